@@ -1,0 +1,447 @@
+#!/usr/bin/env python
+"""FA-KLA prefill benchmark (one JSON line on rank 0).
+
+Workload per GPU (the reference's config 2): FA-KLA prefill, bf16 activations,
+fp32 state, causal, B=8, H=16, T=4096, Dk=Dv=M=128, feature map
+LearnablePositiveMap(2048 -> 2048) fused (phi(q), phi(k), then the chunked
+scan); synthetic q, k, v ~ N(0,1)/sqrt(128) from a seed, map parameters
+initialised like the reference module from torch.manual_seed(0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU. (b, h) sequences are
+independent, so each rank processes its own batch of 8 sequences (weak
+scaling, no collective on the data path); the step time is the max over
+ranks. `value` is all ranks' tokens / that time.
+
+Also reported: `e2e` (the same metric through the public API with pinned host
+buffers, host<->device copies inside the timed region), per-kernel times and
+the roofline of the dominant kernel, the recurrent decode step (config 4) in
+tokens/s and HBM GB/s, the CPU baseline (the reference's own CPU kernel,
+compiled from its sources into oracle/_ref, timed on a bounded sample on this
+host), SM clocks sampled through NVML during the timed region.
+`--impl reference` times the reference's CPU implementation alone (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+B, T, H, D = 8, 4096, 16, 128
+IN_DIM = H * D
+DEC_N, DEC_H, DEC_STEPS = 256, 32, 1024
+DEC_IN = DEC_H * D
+METRIC = "FA-KLA prefill tokens/s"
+UNIT = "tokens/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.isfile(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, interval_s: float = 0.002):
+        self.idx = device_index
+        self.interval = interval_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": "NVML unavailable" if not self.ok else "no samples"}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- helpers
+def lpm_init(in_dim, feat, seed=0):
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    torch.manual_seed(seed)
+    m = LearnablePositiveMap(in_dim, feat)
+    return m.weight.detach().clone(), m.bias.detach().clone()
+
+
+def sync_barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_loop(fn, steps, stream):
+    """Device time (ms) of `steps` calls of fn on `stream`, events on that stream."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_reference_sample(t_len: int, threads: int | None = None):
+    """The reference's CPU path on one sequence batch element: phi with torch
+    fp32 (LearnablePositiveMap = nn.Linear + elu+1, feature_maps.py:259-268) and
+    the reference's own fa_kla_attention_cpu (cpu_kernels.cpp:36-170) from
+    oracle/_ref. Returns (tokens, seconds, kind, cores)."""
+    from oracle import build_ref
+
+    if threads:
+        torch.set_num_threads(threads)
+    cores = torch.get_num_threads()
+    W, b = lpm_init(IN_DIM, H * D)
+    g = torch.Generator().manual_seed(1234)
+    q = torch.randn(1, t_len, IN_DIM, generator=g) / math.sqrt(D)
+    k = torch.randn(1, t_len, IN_DIM, generator=g) / math.sqrt(D)
+    v = (torch.randn(1, t_len, H, D, generator=g) / math.sqrt(D)).contiguous()
+    temp = torch.ones(1, t_len, H)
+    try:
+        ref = build_ref.load()
+        kind = "reference"
+        attn = ref.fa_kla_attention_cpu
+    except Exception:
+        from oracle import fakla_oracle as O
+
+        kind = "port"
+
+        def attn(qm, km, vv, tp):
+            return torch.from_numpy(O.attention(qm.numpy(), km.numpy(), vv.numpy(), tp.numpy(), precision="f32")[0])
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        pq = (torch.nn.functional.elu(torch.nn.functional.linear(q, W, b)) + 1.0).reshape(1, t_len, H, D).contiguous()
+        pk = (torch.nn.functional.elu(torch.nn.functional.linear(k, W, b)) + 1.0).reshape(1, t_len, H, D).contiguous()
+        out = attn(pq, pk, v, temp)
+    dt = time.perf_counter() - t0
+    assert torch.isfinite(out).all()
+    return t_len, dt, kind, cores
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    t_len = args.ref_tokens
+    for _ in range(args.warmup):
+        cpu_reference_sample(t_len)
+    secs = []
+    kind = cores = None
+    for _ in range(args.steps):
+        n, dt, kind, cores = cpu_reference_sample(t_len)
+        secs.append(dt)
+    total = sum(secs)
+    value = args.steps * t_len / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"1 sequence batch element x T={t_len} tokens x H=16 heads per step "
+                                   "(phi torch fp32 + reference fa_kla_attention_cpu); tokens/s is "
+                                   "independent of T for this O(T) recurrence"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(world):
+    return {
+        "workload": "FA-KLA prefill per GPU: B=8, H=16, T=4096, Dk=Dv=M=128, bf16 in / fp32 state, causal, "
+                    "chunk 128, phi = LearnablePositiveMap(2048->2048, elu+1) fused",
+        "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
+        "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
+        "l2": "inputs larger than L2 (q,k,v 403 MB + phi workspace 268 MB per step)",
+    }
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-tokens", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from pulsartecture_b200 import _lib
+    from pulsartecture_b200.attention import fa_kla
+
+    L = _lib.lib()
+    hbm_gbs, tflops_burst, tflops_sust, peak_kind = peaks()
+
+    # ---- inputs (this rank's batch shard; weak scaling)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    q = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    k = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    v = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    W, bias = lpm_init(IN_DIM, H * D)
+    W, bias = W.bfloat16().to(dev), bias.bfloat16().to(dev)
+    out = torch.empty(B, T, H, D, device=dev, dtype=torch.bfloat16)
+    S = torch.empty(B, H, D, D, device=dev, dtype=torch.float32)
+    z = torch.empty(B, H, D, device=dev, dtype=torch.float32)
+    ws_bytes = L.fakla_prefill_workspace_bytes(B, T, IN_DIM, H, D, D, _lib.FAKLA_BF16)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step():
+        _lib.check(L.fakla_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), None, W.data_ptr(), bias.data_ptr(),
+                                   out.data_ptr(), S.data_ptr(), z.data_ptr(), B, T, IN_DIM, H, D, D,
+                                   _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, ws.data_ptr(), ws_bytes, sh))
+
+    for _ in range(args.warmup):
+        step()
+    sync_barrier(world)
+    sampler = ClockSampler(local)
+    with sampler:
+        ms = time_loop(step, args.steps, stream)
+    sync_barrier(world)
+    ms = max_over_ranks(ms, world, dev)
+    ms_per_step = ms / args.steps
+    tokens = B * T * world * args.steps
+    value = tokens / (ms / 1000.0)
+    _lib.check(L.fakla_device_status(sh))
+
+    # ---- per-kernel device times (same shapes, launched alone)
+    phq = ws.data_ptr()
+    phk = ws.data_ptr() + ws_bytes // 2
+    rows2 = 2 * B * T
+    xq = torch.empty(rows2, IN_DIM, device=dev, dtype=torch.bfloat16)
+    xq[: B * T].copy_(q.reshape(B * T, IN_DIM))
+    xq[B * T:].copy_(k.reshape(B * T, IN_DIM))
+
+    def phi_only():
+        _lib.check(L.fakla_phi(xq.data_ptr(), W.data_ptr(), bias.data_ptr(), None, phq, rows2, IN_DIM, H * D, H,
+                               _lib.FAKLA_BF16, sh))
+
+    def scan_only():
+        _lib.check(L.fakla_attention(phq, phk, v.data_ptr(), None, out.data_ptr(), S.data_ptr(), z.data_ptr(),
+                                     B, T, H, D, D, _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, None, 0, sh))
+
+    for _ in range(3):
+        phi_only()
+        scan_only()
+    torch.cuda.synchronize()
+    ksteps = max(args.steps, 20)
+    phi_ms = time_loop(phi_only, ksteps, stream) / ksteps
+    scan_ms = time_loop(scan_only, ksteps, stream) / ksteps
+    del xq
+    phi_flops = 2.0 * rows2 * IN_DIM * (H * D)
+    phi_tflops = phi_flops / (phi_ms * 1e-3) / 1e12
+    scan_bytes = (3 * B * T * H * D * 2) + (B * T * H * D * 2) + B * H * (D * D + D) * 4
+    scan_gbs = scan_bytes / (scan_ms * 1e-3) / 1e9
+    attn_flops = B * T * H * (2 * 128 * D + 2 * 128 * D + 2 * D * D + 2 * D * D + 2 * 128 * D)
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq = q.cpu().pin_memory()
+        hk = k.cpu().pin_memory()
+        hv = v.cpu().pin_memory()
+        hout = torch.empty(B, T, H, D, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            dq = hq.to(dev, non_blocking=True)
+            dk = hk.to(dev, non_blocking=True)
+            dv = hv.to(dev, non_blocking=True)
+            o, _ = fa_kla(dq, dk, dv, phi_weight=W, phi_bias=bias)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        sync_barrier(world)
+        e_steps = max(3, min(args.steps, 10))
+        ems = time_loop(e2e_step, e_steps, stream)
+        sync_barrier(world)
+        ems = max_over_ranks(ems, world, dev)
+        e2e = {"value": B * T * world * e_steps / (ems / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": 3 * B * T * H * D * 2, "d2h_bytes_per_step": B * T * H * D * 2,
+               "ms_per_step": ems / e_steps, "api": "pulsartecture_b200.attention.fa_kla (pinned host in/out)"}
+        del hq, hk, hv, hout
+
+    # ---- decode (config 4): batch 256, H=32, D=M=128, fp32 state, 1024 steps
+    decode = None
+    if not args.no_decode:
+        del ws
+        torch.cuda.empty_cache()
+        gd = torch.Generator(device=dev).manual_seed(2000 + rank)
+        Sd = torch.randn(DEC_N, DEC_H, D, D, generator=gd, device=dev) * 0.02
+        zd = torch.rand(DEC_N, DEC_H, D, generator=gd, device=dev) + 0.5
+        Wd, bd = lpm_init(DEC_IN, DEC_H * D)
+        Wd, bd = Wd.bfloat16().to(dev), bd.bfloat16().to(dev)
+        nsteps = DEC_STEPS
+        qd = (torch.randn(nsteps, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        kd = (torch.randn(nsteps, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        vd = (torch.randn(nsteps, DEC_N, DEC_H, D, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        od = torch.empty(DEC_N, DEC_H, D, device=dev, dtype=torch.bfloat16)
+        dws = L.fakla_decode_workspace_bytes(DEC_N, DEC_IN, DEC_H, D, D, _lib.FAKLA_BF16)
+        dwsb = torch.empty(dws, device=dev, dtype=torch.uint8)
+        it = [0]
+
+        def dstep():
+            i = it[0] % nsteps
+            it[0] += 1
+            _lib.check(L.fakla_decode(qd[i].data_ptr(), kd[i].data_ptr(), vd[i].data_ptr(), None, Wd.data_ptr(),
+                                      bd.data_ptr(), od.data_ptr(), Sd.data_ptr(), zd.data_ptr(), DEC_N, DEC_IN,
+                                      DEC_H, D, D, _lib.FAKLA_BF16, dwsb.data_ptr(), dws, sh))
+
+        phq_d = dwsb.data_ptr()
+        phk_d = dwsb.data_ptr() + dws // 2
+
+        def dstate_only():
+            _lib.check(L.fakla_decode_mapped(phq_d, phk_d, vd[0].data_ptr(), None, od.data_ptr(), Sd.data_ptr(),
+                                             zd.data_ptr(), DEC_N, DEC_H, D, D, _lib.FAKLA_BF16, sh))
+
+        for _ in range(5):
+            dstep()
+        sync_barrier(world)
+        dms = time_loop(dstep, nsteps, stream)
+        sync_barrier(world)
+        dms = max_over_ranks(dms, world, dev)
+        for _ in range(3):
+            dstate_only()
+        st_ms = time_loop(dstate_only, 200, stream) / 200
+        state_bytes = DEC_N * DEC_H * (2 * D * D * 4 + 2 * D * 4 + 2 * D * 2 + D * 2 + D * 2)
+        decode = {
+            "workload": "recurrent decode: batch 256, H=32, Dk=Dv=M=128, fp32 state, 1024 sequential steps, "
+                        "phi LearnablePositiveMap(4096->4096) fused",
+            "tokens_per_s": DEC_N * world * nsteps / (dms / 1000.0), "ms_per_step": dms / nsteps,
+            "state_kernel_us": st_ms * 1000, "state_kernel_gbs": state_bytes / (st_ms * 1e-3) / 1e9,
+            "state_kernel_frac": state_bytes / (st_ms * 1e-3) / 1e9 / hbm_gbs,
+            "state_kernel_bytes": state_bytes, "peak_gbs": hbm_gbs,
+        }
+        del Sd, zd, qd, kd, vd, dwsb
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n, dt, kind, cores = cpu_reference_sample(2048)
+        cpu = {"value": n / dt, "unit": UNIT, "cores": cores, "kind": kind,
+               "sample": "1 batch element x T=2048 tokens x H=16 heads (phi torch fp32 + reference "
+                         "fa_kla_attention_cpu), timed once; tokens/s is independent of T"}
+
+    if rank == 0:
+        clocks = sampler.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)/sqrt(128); map init from seed 0)",
+            "config": workload_config(world),
+            "roofline": {"bound": "tensor", "kernel": "phi_gemm_sm100 (phi(q), phi(k): 2*65536 x 2048 x 2048)",
+                         "achieved": phi_tflops, "peak": tflops_burst, "unit": "TFLOP/s",
+                         "frac": phi_tflops / tflops_burst, "traffic": None,
+                         "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS"},
+            "kernels": {
+                "phi_gemm_sm100": {"ms": phi_ms, "flops": phi_flops, "tflops": phi_tflops,
+                                   "frac_of_peak": phi_tflops / tflops_burst},
+                "scan_sm100": {"ms": scan_ms, "bytes": scan_bytes, "gbs": scan_gbs, "frac_of_hbm": scan_gbs / hbm_gbs,
+                               "tflops": attn_flops / (scan_ms * 1e-3) / 1e12},
+                "sum_ms": phi_ms + scan_ms,
+            },
+            "e2e": e2e,
+            "decode": decode,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,185 @@
+/*
+ * fakla.h -- C ABI of the B200 (sm_100a) FA-KLA library, libfakla.so.
+ *
+ * FA-KLA is Ultra-RWKA's causal, temperature-modulated kernelized linear
+ * attention. For every (batch b, head h) sequence and token t:
+ *
+ *   k~_t  = phi(k_t) * temp_t
+ *   z_t   = z_{t-1} + k~_t                        (normaliser, fp32)
+ *   S_t   = S_{t-1} + k~_t (outer) v_t            (state, fp32, Df x Dv)
+ *   out_t = (phi(q_t)^T S_t) / (phi(q_t) . z_t + 1e-12)
+ *
+ * with phi(x) = elu(x W^T + b) + 1 (LearnablePositiveMap, one linear layer).
+ *
+ * Conventions shared by every entry point:
+ *  - All pointers are device pointers unless stated otherwise. Tensors are
+ *    dense row-major (C-contiguous) in the layouts given per function. The
+ *    activations use the reference's (B, T, H, D) layout.
+ *  - `dtype` selects the element type of the activations (q, k, v, temp, out,
+ *    W, bias): FAKLA_F32 or FAKLA_BF16. The state S, z is always fp32, and all
+ *    accumulation is fp32.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *    asynchronous and stream-ordered; the library keeps no per-call host state,
+ *    so calls on different streams may run concurrently when their buffers are
+ *    disjoint.
+ *  - The caller owns every buffer. Functions that need temporary device memory
+ *    take a caller-provided `workspace` of at least the size reported by the
+ *    matching *_workspace_bytes() query.
+ *  - Return value: FAKLA_OK or a fakla_status error code; nothing is launched
+ *    on error. fakla_last_error() gives a message for the calling thread.
+ *  - There is no CPU path: the library requires an sm_100 device.
+ *
+ * Each declaration names the reference interface it replaces
+ * (0xAEC/Pulsartecture, paths relative to the repository root).
+ */
+#ifndef FAKLA_H_
+#define FAKLA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FAKLA_VERSION 1
+
+typedef enum fakla_dtype {
+  FAKLA_F32 = 0,
+  FAKLA_BF16 = 1
+} fakla_dtype;
+
+typedef enum fakla_status {
+  FAKLA_OK = 0,
+  FAKLA_ERR_INVALID_ARG = 1, /* null pointer, non-positive size, bad flag */
+  FAKLA_ERR_UNSUPPORTED = 2, /* well-formed but outside the implemented set */
+  FAKLA_ERR_ALIGNMENT = 3,   /* a pointer lacks the 16-byte alignment needed */
+  FAKLA_ERR_CUDA = 4,        /* CUDA runtime error while launching */
+  FAKLA_ERR_TIMEOUT = 5,     /* a bounded device-side wait expired */
+  FAKLA_ERR_WORKSPACE = 6,   /* workspace missing or smaller than required */
+  FAKLA_ERR_NO_DEVICE = 7    /* current device is not an sm_100 GPU */
+} fakla_status;
+
+/* Flags for the stateful entry points. */
+#define FAKLA_STATE_IN 1u  /* read the initial (S, z) from the S/z buffers   */
+#define FAKLA_STATE_OUT 2u /* write the final (S, z) to the S/z buffers      */
+
+/* Human-readable name of a status code (static storage). */
+const char* fakla_strerror(int status);
+
+/* Detail message of the last failing call on this host thread ("" if none). */
+const char* fakla_last_error(void);
+
+/* Library ABI version (FAKLA_VERSION). */
+int fakla_version(void);
+
+/*
+ * fakla_attention -- FA-KLA on already feature-mapped q and k.
+ *
+ * Replaces: ultra_rwka.backend.interface.fa_kla_attention(q_mapped, k_mapped,
+ *   v_reshaped, temp), called at ultra_rwka/attention/tm_kla.py:319; its
+ *   native kernels fa_kla_attention_cpu (ultra_rwka/backend/cpp/cpu/
+ *   cpu_kernels.cpp:36) and fa_kla_attention_cuda (ultra_rwka/backend/cuda/
+ *   fa_kla/kernel.cu:627).
+ *
+ *   q_mapped, k_mapped : (B, T, H, Df)   v : (B, T, H, Dv)
+ *   temp               : (B, T, H), or NULL for all ones (tm_kla.py:303-306)
+ *   out                : (B, T, H, Dv), written
+ *   S : (B, H, Df, Dv) fp32, z : (B, H, Df) fp32 -- optional state (NULL with
+ *       flags 0 reproduces the reference exactly: zero initial state, no
+ *       state returned). FAKLA_STATE_IN reads the initial state from S/z;
+ *       FAKLA_STATE_OUT overwrites S/z with the final state. S and z must be
+ *       both NULL or both non-NULL.
+ * Implemented: Df, Dv in [1, 256] on the general path; the tensor-core path
+ * serves dtype BF16 with Df == Dv == 128 and all pointers 16-byte aligned.
+ */
+int fakla_attention(const void* q_mapped, const void* k_mapped, const void* v,
+                    const void* temp, void* out, float* S, float* z, int64_t B,
+                    int64_t T, int64_t H, int64_t Df, int64_t Dv, int dtype,
+                    unsigned flags, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+size_t fakla_attention_workspace_bytes(int64_t B, int64_t T, int64_t H,
+                                       int64_t Df, int64_t Dv, int dtype);
+
+/*
+ * fakla_phi -- the positive feature map phi(x) = elu(x W^T + bias) + 1.
+ *
+ * Replaces: LearnablePositiveMap.forward (ultra_rwka/kernels/feature_maps.py:
+ *   259-268) for num_layers=1, activation='elu+1' (feature_maps.py:224,248).
+ *
+ *   x    : (rows, in_dim)          W : (feat_dim, in_dim) (nn.Linear weight)
+ *   bias : (feat_dim) or NULL      out : (rows, feat_dim), written
+ *   temp : (rows, heads) or NULL; when given, output column n of row r is
+ *          multiplied by temp[r, n / (feat_dim / heads)] (the k-side k*temp
+ *          of cpu_kernels.cpp:121-123 folded into the map).
+ */
+int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
+              void* out, int64_t rows, int64_t in_dim, int64_t feat_dim,
+              int64_t heads, int dtype, void* stream);
+
+/*
+ * fakla_prefill -- feature map fused with FA-KLA: the hot path of
+ * TMLinKernelAttn.forward from the projected q/k/v onward (ultra_rwka/
+ * attention/tm_kla.py:268-332: feature_mapper on q and k, head split,
+ * temperature, fa_kla_attention).
+ *
+ *   q, k : (B, T, in_dim)  projected queries/keys, in_dim = H_total * Dk; the
+ *          feature map mixes all heads of a row, so every row is read whole.
+ *   W    : (H * M, in_dim), bias : (H * M) or NULL -- the rows of the map that
+ *          produce the H heads computed by this call (all heads, or a
+ *          contiguous shard of heads on a multi-GPU run).
+ *   v    : (B, T, H, Dv)   temp : (B, T, H) or NULL   out : (B, T, H, Dv)
+ *   S, z, flags : as fakla_attention, with Df = M.
+ * Needs workspace >= fakla_prefill_workspace_bytes() (holds phi(q), phi(k)).
+ */
+int fakla_prefill(const void* q, const void* k, const void* v, const void* temp,
+                  const void* W, const void* bias, void* out, float* S, float* z,
+                  int64_t B, int64_t T, int64_t in_dim, int64_t H, int64_t M,
+                  int64_t Dv, int dtype, unsigned flags, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim,
+                                     int64_t H, int64_t M, int64_t Dv, int dtype);
+
+/*
+ * fakla_decode_mapped -- one recurrent step for N independent sequences on
+ * already feature-mapped q, k. Reference: none (the reference is stateless,
+ * tm_kla.py:229-337); this is the loop body of cpu_kernels.cpp:121-162 run on
+ * one token with the state injected.
+ *
+ *   q_mapped, k_mapped : (N, H, Df)   v : (N, H, Dv)   temp : (N, H) or NULL
+ *   S : (N, H, Df, Dv) fp32, z : (N, H, Df) fp32 -- read and updated in place
+ *   out : (N, H, Dv), written (uses the updated state, as the reference does)
+ */
+int fakla_decode_mapped(const void* q_mapped, const void* k_mapped, const void* v,
+                        const void* temp, void* out, float* S, float* z, int64_t N,
+                        int64_t H, int64_t Df, int64_t Dv, int dtype, void* stream);
+
+/*
+ * fakla_decode -- feature map fused with one recurrent step: phi(q), phi(k)
+ * from projected rows q, k : (N, in_dim), then fakla_decode_mapped.
+ * W : (H * M, in_dim), bias : (H * M) or NULL; v : (N, H, Dv);
+ * temp : (N, H) or NULL; S : (N, H, M, Dv), z : (N, H, M) updated in place;
+ * out : (N, H, Dv). Needs workspace >= fakla_decode_workspace_bytes().
+ */
+int fakla_decode(const void* q, const void* k, const void* v, const void* temp,
+                 const void* W, const void* bias, void* out, float* S, float* z,
+                 int64_t N, int64_t in_dim, int64_t H, int64_t M, int64_t Dv,
+                 int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fakla_decode_workspace_bytes(int64_t N, int64_t in_dim, int64_t H,
+                                    int64_t M, int64_t Dv, int dtype);
+
+/*
+ * fakla_device_status -- synchronise `stream` and return (then clear) the
+ * device-side status word that kernels set when a bounded wait expires
+ * (FAKLA_ERR_TIMEOUT) or a device-side check fails. FAKLA_OK if clean.
+ */
+int fakla_device_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAKLA_H_ */

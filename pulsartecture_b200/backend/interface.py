@@ -1,0 +1,273 @@
+"""Torch-tensor front end of the FA-KLA C ABI.
+
+Mirrors the reference's backend dispatch for this path:
+``ultra_rwka.backend.interface.fa_kla_attention(q_mapped, k_mapped,
+v_reshaped, temp)`` as called at ultra_rwka/attention/tm_kla.py:319, whose
+native kernel is ``fa_kla_attention_cpu`` (ultra_rwka/backend/cpp/cpu/
+cpu_kernels.cpp:36-170). Same argument meaning, layouts (B, T, H, D), returned
+tensor (a new (B, T, H, Dv) tensor of the input dtype) and error type
+(RuntimeError on a bad shape, dtype or layout).
+
+Differences, all deliberate:
+* inputs must be CUDA tensors on an sm_100 GPU (there is no CPU path);
+* dtypes float32 and bfloat16 (the reference dispatches float/double/half,
+  cpu_kernels.cpp:82; it has no bf16 case);
+* ``temp`` may be None (all ones, the module default at tm_kla.py:303-306);
+* the ``*_with_state`` / prefill / decode entry points carry the recurrent
+  state (S, z), which the reference keeps in locals (cpu_kernels.cpp:78-79).
+
+torch only allocates outputs/workspace and supplies the current stream; all
+arithmetic happens in libfakla.so.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _lib
+
+State = Tuple[torch.Tensor, torch.Tensor]
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.FAKLA_BF16
+    if t.dtype == torch.float32:
+        return _lib.FAKLA_F32
+    raise RuntimeError(f"FA-KLA supports float32 and bfloat16 inputs, got {t.dtype}")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_device(tensors, names) -> torch.device:
+    dev = None
+    for t, n in zip(tensors, names):
+        if t is None:
+            continue
+        _require(t.is_cuda, f"{n} must be a CUDA tensor (libfakla has no CPU path)")
+        if dev is None:
+            dev = t.device
+        _require(t.device == dev, f"{n} is on {t.device}, expected {dev}")
+    return dev
+
+
+def _check_state(state: Optional[State], B: int, H: int, Df: int, Dv: int, dev) -> None:
+    if state is None:
+        return
+    _require(isinstance(state, (tuple, list)) and len(state) == 2, "state must be a (S, z) pair")
+    S, z = state
+    _require(tuple(S.shape) == (B, H, Df, Dv), f"state S must be (B, H, Df, Dv) = {(B, H, Df, Dv)}, got {tuple(S.shape)}")
+    _require(tuple(z.shape) == (B, H, Df), f"state z must be (B, H, Df) = {(B, H, Df)}, got {tuple(z.shape)}")
+    _require(S.dtype == torch.float32 and z.dtype == torch.float32, "state S, z must be float32")
+    _require(S.device == dev and z.device == dev, "state must be on the same device as the inputs")
+    _require(S.is_contiguous() and z.is_contiguous(), "state S, z must be contiguous")
+
+
+def new_state(B: int, H: int, Df: int, Dv: int, device) -> State:
+    """A zero recurrent state (S, z)."""
+    return (torch.zeros(B, H, Df, Dv, device=device, dtype=torch.float32),
+            torch.zeros(B, H, Df, device=device, dtype=torch.float32))
+
+
+def _state_buffers(state: Optional[State], return_state: bool, B, H, Df, Dv, dev):
+    """(S, z, flags) for a functional call: the input state is never mutated."""
+    flags = 0
+    if state is None and not return_state:
+        return None, None, 0
+    if state is not None:
+        S = state[0].clone()
+        z = state[1].clone()
+        flags |= _lib.FAKLA_STATE_IN
+    else:
+        S = torch.empty(B, H, Df, Dv, device=dev, dtype=torch.float32)
+        z = torch.empty(B, H, Df, device=dev, dtype=torch.float32)
+    if return_state:
+        flags |= _lib.FAKLA_STATE_OUT
+    return S, z, flags
+
+
+def fa_kla_attention_with_state(q_mapped: torch.Tensor, k_mapped: torch.Tensor, v_reshaped: torch.Tensor,
+                                temp: Optional[torch.Tensor] = None, state: Optional[State] = None,
+                                return_state: bool = True):
+    """FA-KLA on feature-mapped q, k. Returns ``(out, (S, z))`` (or ``(out, None)``).
+
+    Shapes follow fa_kla_attention_cpu (cpu_kernels.cpp:43-54): q_mapped and
+    k_mapped (B, T, H, Df), v_reshaped (B, T, H, Dv), temp (B, T, H) or None.
+    """
+    _require(q_mapped.dim() == 4, "q_mapped must be 4D (B, T, H, Df)")
+    _require(k_mapped.dim() == 4, "k_mapped must be 4D (B, T, H, Df)")
+    _require(v_reshaped.dim() == 4, "v_reshaped must be 4D (B, T, H, Dv)")
+    _require(temp is None or temp.dim() == 3, "temp must be 3D (B, T, H)")
+    _require(q_mapped.shape == k_mapped.shape, "q_mapped and k_mapped shapes must match")
+    _require(q_mapped.shape[:3] == v_reshaped.shape[:3], "B, T, H dimensions must match for q/k/v")
+    _require(temp is None or tuple(temp.shape) == tuple(q_mapped.shape[:3]),
+             "B, T, H dimensions must match for q/k and temp")
+    dev = _check_device([q_mapped, k_mapped, v_reshaped, temp], ["q_mapped", "k_mapped", "v_reshaped", "temp"])
+    dt = q_mapped.dtype
+    _require(all(t is None or t.dtype == dt for t in (k_mapped, v_reshaped, temp)),
+             "All inputs must have the same dtype")
+    _require(all(t is None or t.is_contiguous() for t in (q_mapped, k_mapped, v_reshaped, temp)),
+             "All input tensors must be contiguous for fa_kla_attention")
+    code = _dtype_code(q_mapped)
+    B, T, H, Df = q_mapped.shape
+    Dv = v_reshaped.shape[3]
+    _check_state(state, B, H, Df, Dv, dev)
+    out = torch.empty_like(v_reshaped)
+    S, z, flags = _state_buffers(state, return_state, B, H, Df, Dv, dev)
+    if B * T * H == 0:
+        return out, ((S, z) if return_state else None)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_attention(
+            _ptr(q_mapped), _ptr(k_mapped), _ptr(v_reshaped), _ptr(temp), _ptr(out), _ptr(S), _ptr(z),
+            B, T, H, Df, Dv, code, flags, None, 0, _stream(dev)))
+    return out, ((S, z) if return_state else None)
+
+
+def fa_kla_attention(q_mapped: torch.Tensor, k_mapped: torch.Tensor, v_reshaped: torch.Tensor,
+                     temp: Optional[torch.Tensor]) -> torch.Tensor:
+    """Drop-in for the reference's ``fa_kla_attention`` (tm_kla.py:15,319):
+    zero initial state, returns only the (B, T, H, Dv) output."""
+    out, _ = fa_kla_attention_with_state(q_mapped, k_mapped, v_reshaped, temp, None, False)
+    return out
+
+
+def phi_map(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+            temp: Optional[torch.Tensor] = None, heads: int = 1) -> torch.Tensor:
+    """phi(x) = elu(x W^T + b) + 1 (LearnablePositiveMap.forward, feature_maps.py:
+    259-268), optionally times temp[..., head]. x: (..., in_dim) -> (..., feat)."""
+    _require(weight.dim() == 2, "weight must be (feat_dim, in_dim)")
+    feat, in_dim = weight.shape
+    _require(x.shape[-1] == in_dim, f"x last dim {x.shape[-1]} != in_dim {in_dim}")
+    _require(bias is None or tuple(bias.shape) == (feat,), "bias must be (feat_dim,)")
+    _require(feat % heads == 0, "feat_dim must be divisible by heads")
+    lead = x.shape[:-1]
+    rows = 1
+    for s in lead:
+        rows *= s
+    _require(temp is None or temp.numel() == rows * heads, "temp must hold one value per (row, head)")
+    dev = _check_device([x, weight, bias, temp], ["x", "weight", "bias", "temp"])
+    dt = x.dtype
+    _require(all(t is None or t.dtype == dt for t in (weight, bias, temp)), "x, weight, bias, temp must share a dtype")
+    code = _dtype_code(x)
+    x = x.contiguous()
+    weight = weight.contiguous()
+    bias = None if bias is None else bias.contiguous()
+    temp = None if temp is None else temp.contiguous()
+    out = torch.empty(*lead, feat, device=dev, dtype=dt)
+    if rows == 0:
+        return out
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_phi(_ptr(x), _ptr(weight), _ptr(bias), _ptr(temp), _ptr(out),
+                               rows, in_dim, feat, heads, code, _stream(dev)))
+    return out
+
+
+def fa_kla_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
+                   bias: Optional[torch.Tensor] = None, temp: Optional[torch.Tensor] = None,
+                   state: Optional[State] = None, return_state: bool = True):
+    """phi fused with FA-KLA (tm_kla.py:268-332 from the projected q/k/v on).
+
+    q, k: (B, T, in_dim) or (B, T, H_in, Dk) projected rows (phi mixes all heads
+    of a row); v: (B, T, H, Dv); weight: (H*M, in_dim) -- the map rows of the H
+    heads computed here; bias: (H*M,) or None; temp: (B, T, H) or None.
+    Returns (out (B, T, H, Dv), (S (B,H,M,Dv), z (B,H,M)) or None).
+    """
+    _require(q.dim() >= 3 and k.shape == q.shape, "q and k must have the same (B, T, ...) shape")
+    _require(v.dim() == 4, "v must be 4D (B, T, H, Dv)")
+    B, T = q.shape[0], q.shape[1]
+    in_dim = 1
+    for s in q.shape[2:]:
+        in_dim *= s
+    _require(tuple(v.shape[:2]) == (B, T), "B, T dimensions must match for q/k/v")
+    H, Dv = v.shape[2], v.shape[3]
+    _require(weight.dim() == 2 and weight.shape[1] == in_dim, f"weight must be (H*M, {in_dim})")
+    _require(weight.shape[0] % H == 0, "weight rows must be divisible by the number of heads")
+    M = weight.shape[0] // H
+    _require(bias is None or tuple(bias.shape) == (H * M,), "bias must be (H*M,)")
+    _require(temp is None or tuple(temp.shape) == (B, T, H), "temp must be (B, T, H)")
+    dev = _check_device([q, k, v, weight, bias, temp], ["q", "k", "v", "weight", "bias", "temp"])
+    dt = q.dtype
+    _require(all(t is None or t.dtype == dt for t in (k, v, weight, bias, temp)), "All inputs must have the same dtype")
+    _require(all(t is None or t.is_contiguous() for t in (q, k, v, weight, bias, temp)), "All inputs must be contiguous")
+    code = _dtype_code(q)
+    _check_state(state, B, H, M, Dv, dev)
+    out = torch.empty(B, T, H, Dv, device=dev, dtype=dt)
+    S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
+    if B * T == 0:
+        return out, ((S, z) if return_state else None)
+    L = _lib.lib()
+    ws_bytes = L.fakla_prefill_workspace_bytes(B, T, in_dim, H, M, Dv, code)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_prefill(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(temp), _ptr(weight), _ptr(bias), _ptr(out), _ptr(S), _ptr(z),
+            B, T, in_dim, H, M, Dv, code, flags, _ptr(ws), ws_bytes, _stream(dev)))
+    return out, ((S, z) if return_state else None)
+
+
+def fa_kla_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: State,
+                       weight: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                       temp: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One recurrent token for N sequences; updates ``state`` IN PLACE.
+
+    With ``weight`` (the map, (H*M, in_dim)): q, k are projected rows (N, in_dim)
+    or (N, H_in, Dk). Without it, q, k are already mapped: (N, H, Df).
+    v: (N, H, Dv); temp: (N, H) or None; state: S (N, H, Df, Dv), z (N, H, Df)
+    fp32. Returns out (N, H, Dv) computed from the updated state (the reference
+    updates S, z before forming the output, cpu_kernels.cpp:121-162).
+    """
+    _require(v.dim() == 3, "v must be 3D (N, H, Dv)")
+    N, H, Dv = v.shape
+    _require(q.shape == k.shape and q.shape[0] == N, "q and k must match and share N with v")
+    S, z = state
+    dev = _check_device([q, k, v, weight, bias, temp, S, z], ["q", "k", "v", "weight", "bias", "temp", "S", "z"])
+    dt = q.dtype
+    _require(all(t is None or t.dtype == dt for t in (k, v, weight, bias, temp)), "All inputs must have the same dtype")
+    _require(all(t is None or t.is_contiguous() for t in (q, k, v, weight, bias, temp)), "All inputs must be contiguous")
+    _require(temp is None or tuple(temp.shape) == (N, H), "temp must be (N, H)")
+    code = _dtype_code(q)
+    out = torch.empty(N, H, Dv, device=dev, dtype=dt)
+    L = _lib.lib()
+    if weight is None:
+        _require(q.dim() == 3 and q.shape[1] == H, "mapped q, k must be (N, H, Df)")
+        Df = q.shape[2]
+        _check_state(state, N, H, Df, Dv, dev)
+        with torch.cuda.device(dev):
+            _lib.check(L.fakla_decode_mapped(_ptr(q), _ptr(k), _ptr(v), _ptr(temp), _ptr(out), _ptr(S), _ptr(z),
+                                             N, H, Df, Dv, code, _stream(dev)))
+        return out
+    in_dim = 1
+    for s in q.shape[1:]:
+        in_dim *= s
+    _require(weight.dim() == 2 and weight.shape[1] == in_dim and weight.shape[0] % H == 0,
+             f"weight must be (H*M, {in_dim})")
+    M = weight.shape[0] // H
+    _require(bias is None or tuple(bias.shape) == (H * M,), "bias must be (H*M,)")
+    _check_state(state, N, H, M, Dv, dev)
+    ws_bytes = L.fakla_decode_workspace_bytes(N, in_dim, H, M, Dv, code)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(temp), _ptr(weight), _ptr(bias), _ptr(out),
+                                  _ptr(S), _ptr(z), N, in_dim, H, M, Dv, code, _ptr(ws), ws_bytes, _stream(dev)))
+    return out
+
+
+def device_status(stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Synchronise and raise if a kernel recorded a device-side failure
+    (e.g. a bounded wait that expired)."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(_lib.lib().fakla_device_status(s.cuda_stream))

@@ -1,0 +1,393 @@
+// C ABI of libfakla.so (declared in include/fakla.h): argument validation,
+// dispatch between the tensor-core (sm_100a tcgen05) and CUDA-core kernels,
+// workspace carving, and error reporting. No allocation happens here: the
+// caller passes every buffer, including the workspace.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "fakla_common.cuh"
+#include "fakla_kernels.h"
+
+// ---------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------
+static thread_local char g_last_error[512];
+
+int fakla_set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fakla_set_error(FAKLA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+extern "C" const char* fakla_strerror(int status) {
+  switch (status) {
+    case FAKLA_OK: return "ok";
+    case FAKLA_ERR_INVALID_ARG: return "invalid argument";
+    case FAKLA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case FAKLA_ERR_ALIGNMENT: return "misaligned pointer";
+    case FAKLA_ERR_CUDA: return "CUDA error";
+    case FAKLA_ERR_TIMEOUT: return "device-side wait timed out";
+    case FAKLA_ERR_WORKSPACE: return "workspace too small";
+    case FAKLA_ERR_NO_DEVICE: return "no sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* fakla_last_error(void) { return g_last_error; }
+
+extern "C" int fakla_version(void) { return FAKLA_VERSION; }
+
+// ---------------------------------------------------------------------------
+// Per-device state: status word address, SM count, sm_100 check.
+// ---------------------------------------------------------------------------
+__device__ int g_device_status_word;
+
+namespace {
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  std::atomic<int> ready{0};
+  int* status = nullptr;
+  int sms = 0;
+  int major = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+DeviceInfo* device_info(int* err) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *err = cuda_fail(e == cudaSuccess ? cudaErrorInvalidDevice : e, "cudaGetDevice");
+    return nullptr;
+  }
+  DeviceInfo* d = &g_dev[dev];
+  if (d->ready.load(std::memory_order_acquire)) return d;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!d->ready.load(std::memory_order_relaxed)) {
+    e = cudaDeviceGetAttribute(&d->major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&d->status, g_device_status_word);
+    if (e != cudaSuccess) {
+      *err = cuda_fail(e, "device query");
+      return nullptr;
+    }
+    d->ready.store(1, std::memory_order_release);
+  }
+  return d;
+}
+
+int require_device(DeviceInfo** out) {
+  int err = FAKLA_OK;
+  DeviceInfo* d = device_info(&err);
+  if (!d) return err;
+  if (d->major != 10)
+    return fakla_set_error(FAKLA_ERR_NO_DEVICE,
+                           "current device has compute capability %d.x; libfakla is built for sm_100a",
+                           d->major);
+  *out = d;
+  return FAKLA_OK;
+}
+}  // namespace
+
+int* fakla_status_word() {
+  int err;
+  DeviceInfo* d = device_info(&err);
+  return d ? d->status : nullptr;
+}
+
+int fakla_sm_count() {
+  int err;
+  DeviceInfo* d = device_info(&err);
+  return d && d->sms > 0 ? d->sms : 148;
+}
+
+extern "C" int fakla_device_status(void* stream) {
+  DeviceInfo* d = nullptr;
+  int rc = require_device(&d);
+  if (rc != FAKLA_OK) return rc;
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int value = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&value, g_device_status_word, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_status_word, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "status word");
+  if (value != FAKLA_OK)
+    return fakla_set_error(value, "device kernel reported: %s", fakla_strerror(value));
+  return FAKLA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled via the runtime's driver entry point
+// ---------------------------------------------------------------------------
+namespace fakla {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
+                       const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                       const cuuint32_t* elem_strides, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  return fn(map, dtype, rank, base, dims, strides, box, elem_strides,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace fakla
+
+// ---------------------------------------------------------------------------
+// Validation helpers
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kMaxHeadDim = 256;
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+inline size_t esize(int dtype) { return dtype == FAKLA_BF16 ? 2 : 4; }
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int check_dtype(int dtype) {
+  if (dtype != FAKLA_F32 && dtype != FAKLA_BF16)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "dtype %d is not FAKLA_F32 or FAKLA_BF16", dtype);
+  return FAKLA_OK;
+}
+
+int check_state(const float* S, const float* z, unsigned flags) {
+  if (flags & ~(FAKLA_STATE_IN | FAKLA_STATE_OUT))
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "unknown flag bits 0x%x", flags);
+  if ((S == nullptr) != (z == nullptr))
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "S and z must be both NULL or both non-NULL");
+  if (flags && S == nullptr)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "state flags given without S/z buffers");
+  return FAKLA_OK;
+}
+
+// The tensor-core scan needs bf16, 128x128 heads and 16-byte aligned tensors
+// (TMA base addresses; every (b,t,h) row is 256 bytes, so rows stay aligned).
+bool use_sm100_scan(int dtype, const void* q, const void* k, const void* v, const void* out,
+                    const float* S, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+  return dtype == FAKLA_BF16 && fakla::scan_sm100_supported(B, T, H, Df, Dv) && aligned16(q) &&
+         aligned16(k) && aligned16(v) && aligned16(out) && (S == nullptr || aligned16(S));
+}
+
+bool use_sm100_phi(int dtype, const void* x0, const void* x1, const void* W, const void* out0,
+                   const void* out1, const void* bias, int64_t rows, int64_t K, int64_t N,
+                   int64_t heads) {
+  return dtype == FAKLA_BF16 && fakla::phi_sm100_supported(rows, K, N, heads) && aligned16(x0) &&
+         (x1 == nullptr || aligned16(x1)) && aligned16(W) && aligned16(out0) &&
+         (out1 == nullptr || aligned16(out1)) && (bias == nullptr || ((uintptr_t)bias & 3u) == 0);
+}
+
+int run_attention(const void* q, const void* k, const void* v, const void* temp, void* out,
+                  float* S, float* z, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv,
+                  int dtype, unsigned flags, cudaStream_t stream, DeviceInfo* d) {
+  if (use_sm100_scan(dtype, q, k, v, out, S, B, T, H, Df, Dv)) {
+    bool enc = false;
+    cudaError_t e = fakla::launch_scan_sm100(q, k, v, temp, out, S, z, B, T, H, flags, stream,
+                                             d->status, &enc);
+    if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+    if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
+    return FAKLA_OK;
+  }
+  if (!fakla::scan_simt_supported(Df, Dv))
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims Df=%lld Dv=%lld unsupported",
+                           (long long)Df, (long long)Dv);
+  cudaError_t e = fakla::launch_scan_simt(dtype, q, k, v, temp, out, S, z, B, T, H, Df, Dv,
+                                          flags, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "scan_simt launch");
+  return FAKLA_OK;
+}
+
+// phi for one or two row sets sharing W (q rows -> out0, k rows -> out1 with temp1).
+int run_phi(const void* x0, const void* x1, const void* W, const void* bias, const void* temp0,
+            const void* temp1, void* out0, void* out1, int64_t rows, int64_t K, int64_t N,
+            int64_t heads, int dtype, cudaStream_t stream, DeviceInfo* d) {
+  if (use_sm100_phi(dtype, x0, x1, W, out0, out1, bias, rows, K, N, heads)) {
+    bool enc = false;
+    cudaError_t e = fakla::launch_phi_sm100(x0, x1, W, bias, temp0, temp1, out0, out1, rows, K,
+                                            N, heads, stream, d->status, &enc);
+    if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+    if (e != cudaSuccess) return cuda_fail(e, "phi_sm100 launch");
+    return FAKLA_OK;
+  }
+  cudaError_t e = fakla::launch_phi_simt(dtype, x0, W, bias, temp0, out0, rows, K, N, heads, stream);
+  if (e == cudaSuccess && x1 != nullptr)
+    e = fakla::launch_phi_simt(dtype, x1, W, bias, temp1, out1, rows, K, N, heads, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "phi_simt launch");
+  return FAKLA_OK;
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Entry points
+// ---------------------------------------------------------------------------
+extern "C" size_t fakla_attention_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t,
+                                                  int) {
+  return 0;
+}
+
+extern "C" int fakla_attention(const void* q, const void* k, const void* v, const void* temp,
+                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                               int64_t Df, int64_t Dv, int dtype, unsigned flags, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !out)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "q_mapped, k_mapped, v and out must be non-NULL");
+  if (B < 1 || T < 1 || H < 1 || Df < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive (B=%lld T=%lld H=%lld Df=%lld Dv=%lld)",
+                           (long long)B, (long long)T, (long long)H, (long long)Df, (long long)Dv);
+  if (Df > kMaxHeadDim || Dv > kMaxHeadDim)
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
+  if ((rc = check_state(S, z, flags))) return rc;
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  return run_attention(q, k, v, temp, out, S, z, B, T, H, Df, Dv, dtype, flags,
+                       (cudaStream_t)stream, d);
+}
+
+extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
+                         void* out, int64_t rows, int64_t in_dim, int64_t feat_dim,
+                         int64_t heads, int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!x || !W || !out)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "x, W and out must be non-NULL");
+  if (rows < 1 || in_dim < 1 || feat_dim < 1 || heads < 1 || feat_dim % heads != 0)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG,
+                           "bad sizes rows=%lld in_dim=%lld feat_dim=%lld heads=%lld",
+                           (long long)rows, (long long)in_dim, (long long)feat_dim, (long long)heads);
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  return run_phi(x, nullptr, W, bias, temp, nullptr, out, nullptr, rows, in_dim, feat_dim, heads,
+                 dtype, (cudaStream_t)stream, d);
+}
+
+extern "C" size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim, int64_t H,
+                                                int64_t M, int64_t Dv, int dtype) {
+  (void)in_dim;
+  (void)Dv;
+  if (B < 1 || T < 1 || H < 1 || M < 1) return 0;
+  const size_t one = round_up((size_t)B * (size_t)T * (size_t)H * (size_t)M * esize(dtype), 256);
+  return 2 * one;
+}
+
+extern "C" int fakla_prefill(const void* q, const void* k, const void* v, const void* temp,
+                             const void* W, const void* bias, void* out, float* S, float* z,
+                             int64_t B, int64_t T, int64_t in_dim, int64_t H, int64_t M,
+                             int64_t Dv, int dtype, unsigned flags, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !W || !out)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "q, k, v, W and out must be non-NULL");
+  if (B < 1 || T < 1 || in_dim < 1 || H < 1 || M < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if (M > kMaxHeadDim || Dv > kMaxHeadDim)
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
+  if ((rc = check_state(S, z, flags))) return rc;
+  const size_t need = fakla_prefill_workspace_bytes(B, T, in_dim, H, M, Dv, dtype);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fakla_set_error(FAKLA_ERR_WORKSPACE, "prefill needs %zu workspace bytes, got %zu", need,
+                           workspace == nullptr ? (size_t)0 : workspace_bytes);
+  if (!aligned16(workspace))
+    return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t rows = B * T;
+  uint8_t* ws = (uint8_t*)workspace;
+  void* phq = ws;
+  void* phk = ws + need / 2;
+  // phi(q) and phi(k)*temp in one launch (k-side temperature fused, so the
+  // scan below runs with temp = NULL).
+  rc = run_phi(q, k, W, bias, nullptr, temp, phq, phk, rows, in_dim, H * M, H, dtype, st, d);
+  if (rc) return rc;
+  return run_attention(phq, phk, v, nullptr, out, S, z, B, T, H, M, Dv, dtype, flags, st, d);
+}
+
+extern "C" int fakla_decode_mapped(const void* q, const void* k, const void* v, const void* temp,
+                                   void* out, float* S, float* z, int64_t N, int64_t H,
+                                   int64_t Df, int64_t Dv, int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !out || !S || !z)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "q, k, v, out, S and z must be non-NULL");
+  if (N < 1 || H < 1 || Df < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if (Df > kMaxHeadDim || Dv > kMaxHeadDim)
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_decode(dtype, q, k, v, temp, out, S, z, N * H, Df, Dv,
+                                       (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return FAKLA_OK;
+}
+
+extern "C" size_t fakla_decode_workspace_bytes(int64_t N, int64_t in_dim, int64_t H, int64_t M,
+                                               int64_t Dv, int dtype) {
+  (void)in_dim;
+  (void)Dv;
+  if (N < 1 || H < 1 || M < 1) return 0;
+  return 2 * round_up((size_t)N * (size_t)H * (size_t)M * esize(dtype), 256);
+}
+
+extern "C" int fakla_decode(const void* q, const void* k, const void* v, const void* temp,
+                            const void* W, const void* bias, void* out, float* S, float* z,
+                            int64_t N, int64_t in_dim, int64_t H, int64_t M, int64_t Dv, int dtype,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !W || !out || !S || !z)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "q, k, v, W, out, S and z must be non-NULL");
+  if (N < 1 || in_dim < 1 || H < 1 || M < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if (M > kMaxHeadDim || Dv > kMaxHeadDim)
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
+  const size_t need = fakla_decode_workspace_bytes(N, in_dim, H, M, Dv, dtype);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fakla_set_error(FAKLA_ERR_WORKSPACE, "decode needs %zu workspace bytes, got %zu", need,
+                           workspace == nullptr ? (size_t)0 : workspace_bytes);
+  if (!aligned16(workspace))
+    return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  void* phq = ws;
+  void* phk = ws + need / 2;
+  rc = run_phi(q, k, W, bias, nullptr, temp, phq, phk, N, in_dim, H * M, H, dtype, st, d);
+  if (rc) return rc;
+  cudaError_t e = fakla::launch_decode(dtype, phq, phk, v, nullptr, out, S, z, N * H, M, Dv, st);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return FAKLA_OK;
+}

@@ -1,0 +1,53 @@
+// Shared device/host helpers for the FA-KLA kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/fakla.h"
+
+namespace fakla {
+
+// Stability constant of the denominator: K_EPSILON in the reference's CPU
+// kernel (ultra_rwka/backend/cpp/cpu/cpu_kernels.cpp:22), used for fp32 and
+// bf16 activations alike (accumulation is fp32 in both).
+constexpr float kEps = 1e-12f;
+
+// Kernels that wait (bounded) receive a pointer to the device-side status word
+// (defined in fakla_api.cu, one per device) and record the first failure in it
+// with atomicCAS(0 -> code); fakla_device_status() reads and clears it.
+__device__ __forceinline__ void report_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// phi activation: elu(x) + 1 = x + 1 for x > 0, exp(x) for x <= 0.
+// (F.elu(x) + 1.0 with alpha = 1, ultra_rwka/kernels/feature_maps.py:248.)
+__device__ __forceinline__ float elu_plus_one(float x) {
+  return x > 0.f ? x + 1.f : expf(x);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+}  // namespace fakla
+
+// Host-side helpers defined in fakla_api.cu.
+int fakla_set_error(int status, const char* fmt, ...);
+int* fakla_status_word();  // device address of the current device's status word
+int fakla_sm_count();      // SM count of the current device (cached)

@@ -1,0 +1,41 @@
+// Internal launcher declarations shared by the kernel files and the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fakla {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank,
+                       void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                       const cuuint32_t* box, const cuuint32_t* elem_strides,
+                       CUtensorMapSwizzle swizzle);
+
+// CUDA-core kernels (simt_kernels.cu)
+cudaError_t launch_phi_simt(int dtype, const void* x, const void* W, const void* bias,
+                            const void* temp, void* out, int64_t rows, int64_t K, int64_t N,
+                            int64_t heads, cudaStream_t stream);
+bool scan_simt_supported(int64_t Df, int64_t Dv);
+size_t scan_simt_smem_bytes(int64_t Df, int64_t Dv);
+cudaError_t launch_scan_simt(int dtype, const void* q, const void* k, const void* v,
+                             const void* temp, void* out, float* S, float* z, int64_t B,
+                             int64_t T, int64_t H, int64_t Df, int64_t Dv, unsigned flags,
+                             cudaStream_t stream);
+cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v,
+                          const void* temp, void* out, float* S, float* z, int64_t NH,
+                          int64_t Df, int64_t Dv, cudaStream_t stream);
+
+// Tensor-core kernels (sm100_phi.cu, sm100_scan.cu); bf16 only.
+bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads);
+cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
+                             const void* temp0, const void* temp1, void* out0, void* out1,
+                             int64_t rows, int64_t K, int64_t N, int64_t heads,
+                             cudaStream_t stream, int* status, bool* encoded);
+bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
+cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
+                              void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                              unsigned flags, cudaStream_t stream, int* status, bool* encoded);
+
+}  // namespace fakla

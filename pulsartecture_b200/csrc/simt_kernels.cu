@@ -1,0 +1,397 @@
+// General-shape FA-KLA kernels on the CUDA cores (fp32 arithmetic).
+//
+// These serve (a) the fp32 precision mode, whose 1e-5 relative-L2 bar rules
+// out bf16/tf32 tensor-core operands, and (b) bf16 shapes outside the tile set
+// of the tensor-core kernels (head dims other than 128, unaligned pointers).
+// The decode kernel here is the production decode path for every dtype: one
+// decode step is a read-modify-write stream over the fp32 state, bound by HBM.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fakla_common.cuh"
+#include "fakla_kernels.h"
+
+namespace fakla {
+
+// ---------------------------------------------------------------------------
+// phi(x) = elu(x W^T + b) + 1, optionally times temp[row, head]: tiled fp32
+// GEMM (64x64 output tile, 256 threads, 4x4 outputs per thread, K step 16).
+// x: (rows, K) row-major, W: (N, K) row-major (nn.Linear weight).
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kPhiTile = 64;
+constexpr int kPhiK = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) phi_simt_kernel(
+    const T* __restrict__ x, const T* __restrict__ W, const T* __restrict__ bias,
+    const T* __restrict__ temp, T* __restrict__ out, int64_t rows, int64_t K,
+    int64_t N, int64_t heads) {
+  __shared__ float xs[kPhiK][kPhiTile + 4];
+  __shared__ float ws[kPhiK][kPhiTile + 4];
+  const int tid = threadIdx.x;
+  const int64_t row0 = (int64_t)blockIdx.y * kPhiTile;
+  const int64_t col0 = (int64_t)blockIdx.x * kPhiTile;
+  const int tr = tid / 16, tc = tid % 16;  // 16x16 threads, 4x4 outputs each
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += kPhiK) {
+    // 64 rows x 16 k per operand = 1024 elements, 4 per thread.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      const int r = e / kPhiK, kk = e % kPhiK;
+      const int64_t gk = k0 + kk;
+      const int64_t gr = row0 + r, gc = col0 + r;
+      xs[kk][r] = (gr < rows && gk < K) ? to_f32(x[gr * K + gk]) : 0.f;
+      ws[kk][r] = (gc < N && gk < K) ? to_f32(W[gc * K + gk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kPhiK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = xs[kk][tr * 4 + i];
+        b[i] = ws[kk][tc * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  const int64_t m = N / heads;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gr = row0 + tr * 4 + i;
+    if (gr >= rows) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gc = col0 + tc * 4 + j;
+      if (gc >= N) continue;
+      float val = acc[i][j] + (bias ? to_f32(bias[gc]) : 0.f);
+      val = elu_plus_one(val);
+      if (temp) val *= to_f32(temp[gr * heads + gc / m]);
+      out[gr * N + gc] = from_f32<T>(val);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Causal FA-KLA scan, one CTA per (b,h) sequence, token-sequential.
+// Thread (g, dv) keeps S[f][dv] for f = g, g+G, g+2G, ... in registers
+// (G = 256 / Dv feature groups) and its slice of z; per token it updates its
+// state and produces partial numerator/denominator sums that are reduced
+// across the G groups in shared memory, kTok tokens at a time.
+// Follows the recurrence of cpu_kernels.cpp:107-164 with fp32 state.
+// ---------------------------------------------------------------------------
+constexpr int kTok = 16;
+constexpr int kScanMaxF = 64;  // features per thread (register array bound)
+
+template <typename T>
+__global__ void __launch_bounds__(256) scan_simt_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+    const T* __restrict__ temp, T* __restrict__ out, float* __restrict__ S,
+    float* __restrict__ z, int64_t T_len, int64_t H, int Df, int Dv, unsigned flags) {
+  extern __shared__ float smem[];
+  float* qs = smem;                  // [kTok][Df]
+  float* ks = qs + kTok * Df;        // [kTok][Df]  (k * temp)
+  float* vs = ks + kTok * Df;        // [kTok][Dv]
+  const int G = 256 / Dv;            // >= 1 (Dv <= 256)
+  float* pn = vs + kTok * Dv;        // [kTok][G][Dv]
+  float* pd = pn + kTok * G * Dv;    // [kTok][G]
+
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / H, h = bh % H;
+  const int tid = threadIdx.x;
+  const int g = tid / Dv, dv = tid % Dv;
+  const bool active = g < G;
+  const int nf = (Df + G - 1) / G;
+
+  float s[kScanMaxF];
+  float zr[kScanMaxF];
+#pragma unroll
+  for (int i = 0; i < kScanMaxF; ++i) {
+    s[i] = 0.f;
+    zr[i] = 0.f;
+    const int f = g + i * G;
+    if (active && i < nf && f < Df && (flags & FAKLA_STATE_IN)) {
+      s[i] = S[(bh * Df + f) * Dv + dv];
+      zr[i] = z[bh * Df + f];
+    }
+  }
+
+  for (int64_t t0 = 0; t0 < T_len; t0 += kTok) {
+    const int nt = (int)(T_len - t0 < kTok ? T_len - t0 : kTok);
+    for (int e = tid; e < nt * Df; e += blockDim.x) {
+      const int tt = e / Df, f = e % Df;
+      const int64_t row = (b * T_len + t0 + tt) * H + h;
+      const float tp = temp ? to_f32(temp[row]) : 1.f;
+      qs[tt * Df + f] = to_f32(q[row * Df + f]);
+      ks[tt * Df + f] = to_f32(k[row * Df + f]) * tp;
+    }
+    for (int e = tid; e < nt * Dv; e += blockDim.x) {
+      const int tt = e / Dv, d = e % Dv;
+      const int64_t row = (b * T_len + t0 + tt) * H + h;
+      vs[tt * Dv + d] = to_f32(v[row * Dv + d]);
+    }
+    __syncthreads();
+    if (active) {
+      for (int tt = 0; tt < nt; ++tt) {
+        const float vv = vs[tt * Dv + dv];
+        float an = 0.f, ad = 0.f;
+#pragma unroll
+        for (int i = 0; i < kScanMaxF; ++i) {
+          const int f = g + i * G;
+          if (i < nf && f < Df) {
+            const float kt = ks[tt * Df + f];
+            const float qq = qs[tt * Df + f];
+            zr[i] += kt;
+            s[i] = fmaf(kt, vv, s[i]);
+            an = fmaf(qq, s[i], an);
+            ad = fmaf(qq, zr[i], ad);
+          }
+        }
+        pn[(tt * G + g) * Dv + dv] = an;
+        if (dv == 0) pd[tt * G + g] = ad;
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < nt * Dv; e += blockDim.x) {
+      const int tt = e / Dv, d = e % Dv;
+      float num = 0.f, den = 0.f;
+      for (int gg = 0; gg < G; ++gg) {
+        num += pn[(tt * G + gg) * Dv + d];
+        den += pd[tt * G + gg];
+      }
+      const int64_t row = (b * T_len + t0 + tt) * H + h;
+      out[row * Dv + d] = from_f32<T>(num * (1.f / (den + kEps)));
+    }
+    __syncthreads();
+  }
+
+  if (flags & FAKLA_STATE_OUT) {
+#pragma unroll
+    for (int i = 0; i < kScanMaxF; ++i) {
+      const int f = g + i * G;
+      if (active && i < nf && f < Df) {
+        S[(bh * Df + f) * Dv + dv] = s[i];
+        if (dv == 0) z[bh * Df + f] = zr[i];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Decode: one token for each of N*H sequences, state updated in place.
+// One CTA per (n,h). Each row f of S (Dv floats) is handled by TPR = Dv/VEC
+// threads with VEC-wide loads; the CTA covers RPP = 256/TPR rows per pass.
+// S is read once and written once with streaming (evict-first) accesses:
+//   S' = S + k~ (outer) v ;  z' = z + k~ ;  out = (phi_q^T S') / (phi_q . z' + eps)
+// ---------------------------------------------------------------------------
+template <int VEC>
+struct VecF;
+template <>
+struct VecF<4> {
+  using type = float4;
+};
+template <>
+struct VecF<1> {
+  using type = float;
+};
+
+__device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ float ld_stream(const float* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_stream(float* p, float v) { __stcs(p, v); }
+
+__device__ __forceinline__ float4 upd(float4 s, float kt, float4 v) {
+  return make_float4(fmaf(kt, v.x, s.x), fmaf(kt, v.y, s.y), fmaf(kt, v.z, s.z),
+                     fmaf(kt, v.w, s.w));
+}
+__device__ __forceinline__ float upd(float s, float kt, float v) { return fmaf(kt, v, s); }
+__device__ __forceinline__ void acc_add(float4& a, float q, float4 s) {
+  a.x = fmaf(q, s.x, a.x);
+  a.y = fmaf(q, s.y, a.y);
+  a.z = fmaf(q, s.z, a.z);
+  a.w = fmaf(q, s.w, a.w);
+}
+__device__ __forceinline__ void acc_add(float& a, float q, float s) { a = fmaf(q, s, a); }
+__device__ __forceinline__ void zero(float4& a) { a = make_float4(0.f, 0.f, 0.f, 0.f); }
+__device__ __forceinline__ void zero(float& a) { a = 0.f; }
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) decode_kernel(
+    const T* __restrict__ qm, const T* __restrict__ km, const T* __restrict__ v,
+    const T* __restrict__ temp, T* __restrict__ out, float* __restrict__ S,
+    float* __restrict__ z, int Df, int Dv) {
+  using V = typename VecF<VEC>::type;
+  extern __shared__ float smem[];
+  const int df4 = (Df + 3) & ~3, dv4 = (Dv + 3) & ~3;  // keep float4 views 16B-aligned
+  float* phq = smem;        // [Df]
+  float* kt = phq + df4;    // [Df]
+  float* vv = kt + df4;     // [Dv]
+  float* part = vv + dv4;   // [RPP][Dv]
+  __shared__ float den_part[8];
+
+  const int64_t bh = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int TPR = Dv / VEC;
+  const int RPP = 256 / TPR;
+  const int lane = tid % TPR, rg = tid / TPR;
+  const float tp = temp ? to_f32(temp[bh]) : 1.f;
+  for (int f = tid; f < Df; f += 256) {
+    phq[f] = to_f32(qm[bh * Df + f]);
+    kt[f] = to_f32(km[bh * Df + f]) * tp;
+  }
+  for (int d = tid; d < Dv; d += 256) vv[d] = to_f32(v[bh * Dv + d]);
+  __syncthreads();
+
+  // Normaliser: z' = z + k~, den = phi_q . z'.
+  float dpart = 0.f;
+  for (int f = tid; f < Df; f += 256) {
+    const float zn = z[bh * Df + f] + kt[f];
+    z[bh * Df + f] = zn;
+    dpart = fmaf(phq[f], zn, dpart);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dpart += __shfl_xor_sync(0xffffffffu, dpart, o);
+  if ((tid & 31) == 0) den_part[tid >> 5] = dpart;
+
+  V acc;
+  zero(acc);
+  if (rg < RPP) {
+    const V vr = *reinterpret_cast<const V*>(vv + lane * VEC);
+    V* base = reinterpret_cast<V*>(S + bh * (int64_t)Df * Dv) + lane;
+    const int vstride = Dv / VEC;
+    int f = rg;
+    // 8 rows in flight per thread: issue the loads, then update/store.
+    for (; f + 7 * RPP < Df; f += 8 * RPP) {
+      V sv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sv[i] = ld_stream(base + (int64_t)(f + i * RPP) * vstride);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int ff = f + i * RPP;
+        sv[i] = upd(sv[i], kt[ff], vr);
+        st_stream(base + (int64_t)ff * vstride, sv[i]);
+        acc_add(acc, phq[ff], sv[i]);
+      }
+    }
+    for (; f < Df; f += RPP) {
+      V sv = ld_stream(base + (int64_t)f * vstride);
+      sv = upd(sv, kt[f], vr);
+      st_stream(base + (int64_t)f * vstride, sv);
+      acc_add(acc, phq[f], sv);
+    }
+    *reinterpret_cast<V*>(part + rg * Dv + lane * VEC) = acc;
+  }
+  __syncthreads();
+  float den = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) den += den_part[w];
+  const float inv = 1.f / (den + kEps);
+  for (int d = tid; d < Dv; d += 256) {
+    float num = 0.f;
+    for (int r = 0; r < RPP; ++r) num += part[r * Dv + d];
+    out[bh * Dv + d] = from_f32<T>(num * inv);
+  }
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Launchers (host). Shapes were validated by the caller (fakla_api.cu).
+// ---------------------------------------------------------------------------
+template <typename T>
+static cudaError_t launch_phi_simt_t(const void* x, const void* W, const void* bias,
+                                     const void* temp, void* out, int64_t rows,
+                                     int64_t K, int64_t N, int64_t heads,
+                                     cudaStream_t stream) {
+  dim3 grid((unsigned)((N + kPhiTile - 1) / kPhiTile), (unsigned)((rows + kPhiTile - 1) / kPhiTile));
+  phi_simt_kernel<T><<<grid, 256, 0, stream>>>(
+      (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_phi_simt(int dtype, const void* x, const void* W, const void* bias,
+                            const void* temp, void* out, int64_t rows, int64_t K,
+                            int64_t N, int64_t heads, cudaStream_t stream) {
+  if (dtype == FAKLA_BF16)
+    return launch_phi_simt_t<__nv_bfloat16>(x, W, bias, temp, out, rows, K, N, heads, stream);
+  return launch_phi_simt_t<float>(x, W, bias, temp, out, rows, K, N, heads, stream);
+}
+
+bool scan_simt_supported(int64_t Df, int64_t Dv) {
+  if (Df < 1 || Dv < 1 || Dv > 256 || Df > 256) return false;
+  const int64_t G = 256 / Dv;
+  return (Df + G - 1) / G <= kScanMaxF;
+}
+
+size_t scan_simt_smem_bytes(int64_t Df, int64_t Dv) {
+  const int64_t G = 256 / Dv;
+  return sizeof(float) * (size_t)(2 * kTok * Df + kTok * Dv + kTok * G * Dv + kTok * G);
+}
+
+template <typename T>
+static cudaError_t launch_scan_simt_t(const void* q, const void* k, const void* v,
+                                      const void* temp, void* out, float* S, float* z,
+                                      int64_t B, int64_t T_len, int64_t H, int64_t Df,
+                                      int64_t Dv, unsigned flags, cudaStream_t stream) {
+  const size_t smem = scan_simt_smem_bytes(Df, Dv);
+  cudaError_t e = cudaFuncSetAttribute(scan_simt_kernel<T>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  scan_simt_kernel<T><<<(unsigned)(B * H), 256, smem, stream>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, T_len, H,
+      (int)Df, (int)Dv, flags);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan_simt(int dtype, const void* q, const void* k, const void* v,
+                             const void* temp, void* out, float* S, float* z, int64_t B,
+                             int64_t T_len, int64_t H, int64_t Df, int64_t Dv,
+                             unsigned flags, cudaStream_t stream) {
+  if (dtype == FAKLA_BF16)
+    return launch_scan_simt_t<__nv_bfloat16>(q, k, v, temp, out, S, z, B, T_len, H, Df, Dv,
+                                             flags, stream);
+  return launch_scan_simt_t<float>(q, k, v, temp, out, S, z, B, T_len, H, Df, Dv, flags,
+                                   stream);
+}
+
+template <typename T>
+static cudaError_t launch_decode_t(const void* q, const void* k, const void* v,
+                                   const void* temp, void* out, float* S, float* z,
+                                   int64_t NH, int64_t Df, int64_t Dv, cudaStream_t stream) {
+  // float4 path needs Dv % 4 == 0 and Dv/4 threads per row (<= 256); the state
+  // pointer is 16-byte aligned for every row when S is (checked by the caller).
+  const bool vec4 = (Dv % 4 == 0) && (Dv / 4 <= 256) && (((uintptr_t)S & 15u) == 0);
+  const int tpr = vec4 ? (int)(Dv / 4) : (int)Dv;
+  const int rpp = 256 / tpr;
+  const size_t smem = sizeof(float) * (size_t)(2 * ((Df + 3) & ~3) + ((Dv + 3) & ~3) + rpp * Dv);
+  if (vec4) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, 4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    decode_kernel<T, 4><<<(unsigned)NH, 256, smem, stream>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, 1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    decode_kernel<T, 1><<<(unsigned)NH, 256, smem, stream>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v,
+                          const void* temp, void* out, float* S, float* z, int64_t NH,
+                          int64_t Df, int64_t Dv, cudaStream_t stream) {
+  if (dtype == FAKLA_BF16)
+    return launch_decode_t<__nv_bfloat16>(q, k, v, temp, out, S, z, NH, Df, Dv, stream);
+  return launch_decode_t<float>(q, k, v, temp, out, S, z, NH, Df, Dv, stream);
+}
+
+}  // namespace fakla

@@ -1,0 +1,335 @@
+// phi GEMM on the sm_100a tensor cores: out = elu(x W^T + bias) + 1 [* temp].
+//
+// The feature map of the default FA-KLA configuration is one nn.Linear over
+// the full H*Dk projected row followed by elu+1 (LearnablePositiveMap,
+// ultra_rwka/kernels/feature_maps.py:224,248,259-268); at B=8, T=4096,
+// H*Dk=2048 it is ~90% of the FA-KLA FLOPs. This kernel computes it for up to
+// two row sets in one launch (q rows and k rows share W), with the bias,
+// the elu+1 activation and the k-side temperature (k~ = phi(k) * temp,
+// cpu_kernels.cpp:121-123) fused into the epilogue, and writes bf16.
+//
+// Structure: persistent CTAs (one per SM), 6 warps:
+//   warp 0      TMA producer: 128x64 x-tile + 256x64 W-tile per stage (4 stages)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (128x256x16)
+//   warps 2..5  epilogue: TMEM -> registers -> bias/elu+1/temp -> bf16 ->
+//               128B-swizzled staging -> TMA store (per warp, 32 rows)
+// The 128x256 fp32 accumulator is double-buffered in TMEM (2 x 256 columns),
+// so the epilogue of tile i overlaps the MMAs of tile i+1.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fakla_common.cuh"
+#include "fakla_kernels.h"
+#include "sm100_umma.cuh"
+
+namespace fakla {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK * 2;                 // 16 KB
+constexpr int kBBytes = BN * BK * 2;                 // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;       // 48 KB
+constexpr int kEpiWarps = 4;
+constexpr int kOutWarpBytes = 32 * 128;              // 32 rows x 64 bf16
+constexpr int kOutBytes = kEpiWarps * 2 * kOutWarpBytes;  // 32 KB
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 2 * BN;               // 512
+constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
+
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + (size_t)kStages * kStageBytes + kOutBytes + 256;
+
+struct PhiArgs {
+  const __nv_bfloat16* bias;   // [N] or null
+  const __nv_bfloat16* temp0;  // [rows, heads] or null (row set 0)
+  const __nv_bfloat16* temp1;  // [rows, heads] or null (row set 1)
+  int rows, N, K, heads, nsets;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
+    const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC0,
+    const __grid_constant__ CUtensorMap tmC1, const PhiArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;                                  // kStages x 16 KB
+  uint8_t* sB = smem + kStages * kABytes;              // kStages x 32 KB
+  uint8_t* sOut = sB + kStages * kBBytes;              // 32 KB (1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
+  uint64_t* full = bars;                  // [kStages]
+  uint64_t* empty = bars + kStages;       // [kStages]
+  uint64_t* tfull = bars + 2 * kStages;   // [2]
+  uint64_t* tempty = tfull + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int row_tiles = (args.rows + BM - 1) / BM;
+  const int col_tiles = args.N / BN;
+  const int tiles_per_set = row_tiles * col_tiles;
+  const int total_tiles = tiles_per_set * args.nsets;
+  const int kblocks = args.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA0);
+    tma_prefetch_desc(&tmA1);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC0);
+    tma_prefetch_desc(&tmC1);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+        const int set = tile / tiles_per_set;
+        const int r = tile % tiles_per_set;
+        const int row0 = (r / col_tiles) * BM;
+        const int col0 = (r % col_tiles) * BN;
+        const CUtensorMap* mapA = set == 0 ? &tmA0 : &tmA1;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)) {
+            report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(sA + stage * kABytes, mapA, &full[stage], kb * BK, row0);
+          tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * BK, col0);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, kWaitNs)) {
+          report_status(args.status, FAKLA_ERR_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kWaitNs)) {
+            report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + stage * kABytes), 16, 1024);
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + stage * kBBytes), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 bf16 = 32 bytes along K inside the 128-byte swizzle atom
+            mma_ss(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                   (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int ew = warp - 2; // epilogue warp index (staging buffer owner)
+    uint8_t* stage_buf = sOut + ew * 2 * kOutWarpBytes;
+    const int m = args.N / args.heads;  // features per head
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int chunk_count = 0;
+    for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+      const int set = tile / tiles_per_set;
+      const int r = tile % tiles_per_set;
+      const int row0 = (r / col_tiles) * BM;
+      const int col0 = (r % col_tiles) * BN;
+      const CUtensorMap* mapC = set == 0 ? &tmC0 : &tmC1;
+      const __nv_bfloat16* temp = set == 0 ? args.temp0 : args.temp1;
+      const int grow = row0 + 32 * q + lane;  // this thread's output row
+      if (!mbar_wait(&tfull[acc], acc_phase, kWaitNs)) {
+        report_status(args.status, FAKLA_ERR_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int j = 0; j < BN / 64; ++j) {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(t_row + (uint32_t)(j * 64), v0);
+        tmem_ld32(t_row + (uint32_t)(j * 64 + 32), v1);
+        tmem_ld_wait();
+        if (j == BN / 64 - 1) {
+          // accumulator fully read: hand the buffer back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        const int c0 = col0 + j * 64;
+        float tscale = 1.f;
+        if (temp != nullptr && grow < args.rows)
+          tscale = __bfloat162float(temp[(int64_t)grow * args.heads + c0 / m]);
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = c0 + 2 * i;
+          const uint32_t raw_a = i < 16 ? v0[2 * i] : v1[2 * i - 32];
+          const uint32_t raw_b = i < 16 ? v0[2 * i + 1] : v1[2 * i + 1 - 32];
+          float a = __uint_as_float(raw_a);
+          float b = __uint_as_float(raw_b);
+          if (args.bias != nullptr) {
+            const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(args.bias + c);
+            a += __low2float(bb);
+            b += __high2float(bb);
+          }
+          a = elu_plus_one(a) * tscale;
+          b = elu_plus_one(b) * tscale;
+          packed[i] = pack_bf16x2(a, b);
+        }
+        // Staging buffer (j & 1) of this warp: wait until the TMA store issued
+        // from it two chunks ago has finished reading it.
+        uint8_t* buf = stage_buf + (chunk_count & 1) * kOutWarpBytes;
+        if (lane == 0 && chunk_count >= 2) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 val = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                 packed[4 * c + 3]);
+          *reinterpret_cast<uint4*>(buf + sw128_offset((uint32_t)lane, (uint32_t)(c * 8))) = val;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(mapC, buf, c0, row0 + 32 * q);
+          bulk_commit_group();
+        }
+        ++chunk_count;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static bool make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                        uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                           dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads) {
+  if (rows < 1 || K < BK || N < BN) return false;
+  if (K % BK != 0 || N % BN != 0) return false;
+  if (heads < 1 || N % heads != 0 || (N / heads) % 64 != 0) return false;
+  if (rows > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX / 2 || N > (int64_t)INT32_MAX / 2)
+    return false;
+  return true;
+}
+
+cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
+                             const void* temp0, const void* temp1, void* out0, void* out1,
+                             int64_t rows, int64_t K, int64_t N, int64_t heads,
+                             cudaStream_t stream, int* status, bool* encoded) {
+  CUtensorMap mA0, mA1, mB, mC0, mC1;
+  const int nsets = x1 != nullptr ? 2 : 1;
+  bool ok = make_map_2d(&mA0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) &&
+            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, BN) &&
+            make_map_2d(&mC0, out0, (uint64_t)N, (uint64_t)rows, 64, 32);
+  if (ok && nsets == 2)
+    ok = make_map_2d(&mA1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
+         make_map_2d(&mC1, out1, (uint64_t)N, (uint64_t)rows, 64, 32);
+  else {
+    mA1 = mA0;
+    mC1 = mC0;
+  }
+  *encoded = ok;
+  if (!ok) return cudaErrorInvalidValue;
+  PhiArgs a;
+  a.bias = (const __nv_bfloat16*)bias;
+  a.temp0 = (const __nv_bfloat16*)temp0;
+  a.temp1 = (const __nv_bfloat16*)temp1;
+  a.rows = (int)rows;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.heads = (int)heads;
+  a.nsets = nsets;
+  a.status = status;
+  const int row_tiles = (int)((rows + BM - 1) / BM);
+  const int total = row_tiles * (int)(N / BN) * nsets;
+  const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
+  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  phi_gemm_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mA0, mA1, mB, mC0, mC1, a);
+  return cudaGetLastError();
+}
+
+}  // namespace fakla

@@ -1,0 +1,106 @@
+"""The C ABI library: loads without a GPU, exports every symbol the headers
+declare, and rejects malformed calls before touching a device (CPU only; no
+compute call is made here)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from pulsartecture_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    decls = {}
+    for h in sorted(glob.glob(os.path.join(ROOT, "include", "*.h"))):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?(?:int|size_t|char\s*\*|void)\s*\*?\s*(fakla_\w+)\s*\(([^;]*?)\)\s*;",
+                             text, flags=re.M | re.S):
+            args = m.group(2).strip()
+            n = 0 if args in ("", "void") else len([a for a in args.split(",") if a.strip()])
+            decls[m.group(1)] = n
+    return decls
+
+
+def test_header_declares_the_entry_points():
+    d = declared_functions()
+    for name in ["fakla_attention", "fakla_phi", "fakla_prefill", "fakla_decode", "fakla_decode_mapped",
+                 "fakla_strerror", "fakla_last_error", "fakla_device_status"]:
+        assert name in d, name
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name, nargs in declared_functions().items():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in _lib.SIGNATURES, f"{name} missing from the ctypes signature table"
+        assert len(_lib.SIGNATURES[name][1]) == nargs, f"{name}: header has {nargs} args"
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.fakla_version() == 1
+    for code, name in _lib.STATUS.items():
+        assert lib.fakla_strerror(code)
+    assert lib.fakla_strerror(99) == b"unknown status"
+
+
+def test_library_has_no_unresolved_cuda_runtime_dependency():
+    # static CUDA runtime: the .so must not pin a libcudart.so version
+    import subprocess
+
+    out = subprocess.run(["ldd", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcudart" not in out
+
+
+def test_argument_validation_without_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # bad dtype
+    rc = lib.fakla_attention(p, p, p, None, p, None, None, 1, 1, 1, 8, 8, 7, 0, None, 0, None)
+    assert rc == 1 and b"dtype" in lib.fakla_last_error()
+    # null inputs
+    rc = lib.fakla_attention(None, p, p, None, p, None, None, 1, 1, 1, 8, 8, 0, 0, None, 0, None)
+    assert rc == 1
+    # non-positive sizes
+    rc = lib.fakla_attention(p, p, p, None, p, None, None, 0, 1, 1, 8, 8, 0, 0, None, 0, None)
+    assert rc == 1
+    # head dim beyond the implemented range
+    rc = lib.fakla_attention(p, p, p, None, p, None, None, 1, 1, 1, 512, 8, 0, 0, None, 0, None)
+    assert rc == 2
+    # state flags without state buffers
+    rc = lib.fakla_attention(p, p, p, None, p, None, None, 1, 1, 1, 8, 8, 0, 1, None, 0, None)
+    assert rc == 1
+    # S without z
+    rc = lib.fakla_attention(p, p, p, None, p, p, None, 1, 1, 1, 8, 8, 0, 0, None, 0, None)
+    assert rc == 1
+    # prefill without workspace
+    rc = lib.fakla_prefill(p, p, p, None, p, None, p, None, None, 1, 4, 8, 1, 8, 8, 0, 0, None, 0, None)
+    assert rc == 6
+    # decode needs state
+    rc = lib.fakla_decode_mapped(p, p, p, None, p, None, None, 1, 1, 8, 8, 0, None)
+    assert rc == 1
+
+
+def test_workspace_queries():
+    lib = _lib.lib()
+    B, T, D, H, M, Dv = 8, 4096, 2048, 16, 128, 128
+    assert lib.fakla_prefill_workspace_bytes(B, T, D, H, M, Dv, 1) == 2 * B * T * H * M * 2
+    assert lib.fakla_prefill_workspace_bytes(B, T, D, H, M, Dv, 0) == 2 * B * T * H * M * 4
+    assert lib.fakla_decode_workspace_bytes(256, 4096, 32, 128, 128, 1) == 2 * 256 * 32 * 128 * 2
+    assert lib.fakla_attention_workspace_bytes(B, T, H, M, Dv, 1) == 0
+
+
+def test_call_without_gpu_reports_error_not_crash():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("this checks the no-GPU path")
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+    rc = lib.fakla_attention(p, p, p, None, p, None, None, 1, 1, 1, 8, 8, 0, 0, None, 0, None)
+    assert rc in (4, 7)  # CUDA error (no device) or no sm_100 device

@@ -1,0 +1,160 @@
+"""Fused phi + FA-KLA prefill and the module API against the oracle and the
+reference's golden outputs (GPU only)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fakla_oracle as O
+from tests.helpers import BF16_MAX_ABS, BF16_REL_L2, F32_REL_L2, lpm_params, rel_l2, to_np
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "fakla_golden.npz")
+
+
+def gen(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g)
+
+
+def test_prefill_f32_cfg1_matches_reference_golden(cuda):
+    """Config 1: B=2, H=4, T=256, Dk=Dv=M=64, fp32; LearnablePositiveMap(256,256)
+    from seed 0; output and final state S, z against the reference."""
+    from pulsartecture_b200.attention import fa_kla
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    gold = np.load(GOLDEN)
+    B, T, H, D = 2, 256, 4, 64
+    torch.manual_seed(0)
+    m = LearnablePositiveMap(H * D, H * D).to(cuda)
+    q, k, v = gen((B, T, H, D), 101), gen((B, T, H, D), 102), gen((B, T, H, D), 103)
+    out, (S, z) = fa_kla(q.to(cuda), k.to(cuda), v.to(cuda), phi_weight=m.weight.detach(), phi_bias=m.bias.detach())
+    assert rel_l2(to_np(out), gold["cfg1_out"]) < F32_REL_L2
+    assert rel_l2(to_np(S), gold["cfg1_S"]) < F32_REL_L2
+    assert rel_l2(to_np(z), gold["cfg1_z"]) < F32_REL_L2
+
+
+def test_module_f32_matches_reference_module_golden(cuda):
+    from pulsartecture_b200.attention import TMLinKernelAttn
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    gold = np.load(GOLDEN)
+    torch.manual_seed(0)
+    mapper = LearnablePositiveMap(256, 256)
+    mod = TMLinKernelAttn(256, mapper, num_heads=4, qk_dim=64, v_dim=64)
+    assert sorted(mod.state_dict().keys()) == list(gold["module_state_names"])
+    mod = mod.to(cuda)
+    x = gen((2, 64, 256), 401).to(cuda)
+    with torch.no_grad():
+        y = mod(x)
+    assert y.shape == (2, 64, 256)
+    assert rel_l2(to_np(y), gold["module_out"]) < F32_REL_L2
+
+
+@pytest.mark.parametrize("B,T,H,in_heads,with_temp", [
+    (2, 256, 4, 4, False),
+    (1, 200, 2, 4, True),
+    (2, 1024, 16, 16, False),
+])
+def test_prefill_bf16_fused(cuda, B, T, H, in_heads, with_temp):
+    from pulsartecture_b200.attention import fa_kla
+
+    D = 128
+    in_dim = in_heads * D
+    q = (gen((B, T, in_heads, D), 70) / np.sqrt(D)).bfloat16().to(cuda)
+    k = (gen((B, T, in_heads, D), 71) / np.sqrt(D)).bfloat16().to(cuda)
+    v = (gen((B, T, H, D), 72) / np.sqrt(D)).bfloat16().to(cuda)
+    W, b = lpm_params(in_dim, H * D, seed=73, dtype=torch.bfloat16)
+    tp = None
+    if with_temp:
+        g = torch.Generator().manual_seed(74)
+        tp = (torch.rand(B, T, H, generator=g) + 0.5).bfloat16().to(cuda)
+    out, (S, z) = fa_kla(q, k, v, phi_weight=W.to(cuda), phi_bias=b.to(cuda), temp=tp)
+    eo, eS, ez = O.prefill(to_np(q), to_np(k), to_np(v), to_np(W), to_np(b), None if tp is None else to_np(tp))
+    assert rel_l2(to_np(out), eo) < BF16_REL_L2
+    assert np.abs(to_np(out) - eo).max() < BF16_MAX_ABS
+    assert rel_l2(to_np(S), eS) < BF16_REL_L2
+    assert rel_l2(to_np(z), ez) < BF16_REL_L2
+
+
+def test_prefill_state_handoff_is_exact(cuda):
+    """prefill(T1) then prefill(T2, state) equals prefill(T1+T2) bit for bit when
+    T1 is a multiple of the 128-token chunk (same arithmetic, state in fp32)."""
+    from pulsartecture_b200.attention import fa_kla
+
+    B, T, H, D = 2, 512, 4, 128
+    q = (gen((B, T, H, D), 80) / np.sqrt(D)).bfloat16().to(cuda)
+    k = (gen((B, T, H, D), 81) / np.sqrt(D)).bfloat16().to(cuda)
+    v = (gen((B, T, H, D), 82) / np.sqrt(D)).bfloat16().to(cuda)
+    W, b = lpm_params(H * D, H * D, seed=83, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    full, (S, z) = fa_kla(q, k, v, phi_weight=W, phi_bias=b)
+    o1, st1 = fa_kla(q[:, :256], k[:, :256], v[:, :256], phi_weight=W, phi_bias=b)
+    o2, (S2, z2) = fa_kla(q[:, 256:], k[:, 256:], v[:, 256:], st1, phi_weight=W, phi_bias=b)
+    assert torch.equal(torch.cat([o1, o2], 1), full)
+    assert torch.equal(S2, S) and torch.equal(z2, z)
+
+
+def test_prefill_bf16_cfg2_full_size(cuda):
+    """Config 2 at full size (B=8, H=16, T=4096, D=M=128, bf16): oracle on three
+    (b, h) sequences, size-independent checks on all of them."""
+    from pulsartecture_b200.attention import fa_kla
+    from pulsartecture_b200.backend.interface import phi_map
+
+    B, T, H, D = 8, 4096, 16, 128
+    g = torch.Generator(device=cuda).manual_seed(90)
+    q = (torch.randn(B, T, H, D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    k = (torch.randn(B, T, H, D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    v = (torch.randn(B, T, H, D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    W, b = lpm_params(H * D, H * D, seed=0, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    out, (S, z) = fa_kla(q, k, v, phi_weight=W, phi_bias=b)
+    assert torch.isfinite(out).all() and torch.isfinite(S).all()
+    # z is the column sum of phi(k) over the whole sequence
+    pk = phi_map(k.reshape(B, T, H * D), W, b).float().reshape(B, T, H, D)
+    assert rel_l2(to_np(z), to_np(pk.sum(1))) < 1e-5
+    for bb, hh in [(0, 0), (3, 7), (7, 15)]:
+        Wh, bh = to_np(W)[hh * D:(hh + 1) * D], to_np(b)[hh * D:(hh + 1) * D]
+        pq = O.phi(to_np(q[bb]).reshape(T, H * D), Wh, bh)
+        pkk = O.phi(to_np(k[bb]).reshape(T, H * D), Wh, bh)
+        eo, eS, ez = O.attention(pq[None, :, None], pkk[None, :, None], to_np(v[bb, :, hh])[None, :, None])
+        got = to_np(out[bb, :, hh])
+        assert rel_l2(got, eo[0, :, 0]) < BF16_REL_L2
+        assert np.abs(got - eo[0, :, 0]).max() < BF16_MAX_ABS
+        assert rel_l2(to_np(S[bb, hh]), eS[0, 0]) < BF16_REL_L2
+
+
+def test_module_bf16_fused_path(cuda):
+    from pulsartecture_b200.attention import TMLinKernelAttn
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    torch.manual_seed(1)
+    E, H, D = 512, 4, 128
+    mapper = LearnablePositiveMap(H * D, H * D, dtype=torch.bfloat16)
+    mod = TMLinKernelAttn(E, mapper, num_heads=H, qk_dim=D, v_dim=D, temp_input_dim=32,
+                          dtype=torch.bfloat16).to(cuda)
+    x = (gen((2, 300, E), 95)).bfloat16().to(cuda)
+    ti = gen((2, 300, 32), 96).bfloat16().to(cuda)
+    with torch.no_grad():
+        y, (S, z) = mod(x, temp_input=ti, return_state=True)
+        qp, kp, vp = mod.proj_q(x), mod.proj_k(x), mod.proj_v(x)
+        temp = mod.temp_func(ti).bfloat16()
+    eo, eS, ez = O.prefill(to_np(qp), to_np(kp), to_np(vp).reshape(2, 300, H, D), to_np(mapper.weight),
+                           to_np(mapper.bias), to_np(temp))
+    assert rel_l2(to_np(y).reshape(2, 300, H, D), eo) < BF16_REL_L2
+    # decode continues from the returned state like more prefill would
+    xs = gen((2, E), 97).bfloat16().to(cuda)
+    ts = gen((2, 32), 98).bfloat16().to(cuda)
+    with torch.no_grad():
+        ys = mod.step(xs, (S, z), temp_input=ts)
+        y2 = mod(torch.cat([x, xs[:, None]], 1), temp_input=torch.cat([ti, ts[:, None]], 1))
+    assert rel_l2(to_np(ys), to_np(y2[:, -1])) < BF16_REL_L2
+
+
+def test_native_library_is_loaded(cuda):
+    from pulsartecture_b200 import _lib
+
+    _lib.lib()
+    maps = open("/proc/self/maps").read()
+    assert "libfakla.so" in maps
