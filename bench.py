@@ -230,6 +230,62 @@ def workload_config(world):
     }
 
 
+# ----------------------------------------------------------------------------- single kernel
+def run_only(args):
+    """One kernel of the path alone, on the benchmark's shapes: `phi` = the
+    phi GEMM for q and k of config 2 (2*65536 rows), `scan` = the chunk scan of
+    config 2 on precomputed phi, `decode` = the decode state kernel of config 4.
+    Prints the mean device time per launch."""
+    from pulsartecture_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator(device=dev).manual_seed(7)
+    if args.only in ("phi", "scan"):
+        x = (torch.randn(2 * B * T, IN_DIM, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+        W, bias = lpm_init(IN_DIM, H * D)
+        W, bias = W.bfloat16().to(dev), bias.bfloat16().to(dev)
+        ph = torch.empty(2 * B * T, H * D, device=dev, dtype=torch.bfloat16)
+
+        def phi():
+            _lib.check(L.fakla_phi(x.data_ptr(), W.data_ptr(), bias.data_ptr(), None, ph.data_ptr(),
+                                   2 * B * T, IN_DIM, H * D, H, _lib.FAKLA_BF16, sh))
+        fn = phi
+        if args.only == "scan":
+            phi()
+            v = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+            out = torch.empty_like(v)
+            S = torch.empty(B, H, D, D, device=dev)
+            z = torch.empty(B, H, D, device=dev)
+
+            def scan():
+                _lib.check(L.fakla_attention(ph.data_ptr(), ph[B * T:].data_ptr(), v.data_ptr(), None,
+                                             out.data_ptr(), S.data_ptr(), z.data_ptr(), B, T, H, D, D,
+                                             _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, None, 0, sh))
+            fn = scan
+    else:
+        S = torch.randn(DEC_N, DEC_H, D, D, generator=g, device=dev) * 0.02
+        z = torch.rand(DEC_N, DEC_H, D, generator=g, device=dev) + 0.5
+        qm = (torch.rand(DEC_N, DEC_H, D, generator=g, device=dev) + 0.5).bfloat16()
+        km = (torch.rand(DEC_N, DEC_H, D, generator=g, device=dev) + 0.5).bfloat16()
+        vd = (torch.randn(DEC_N, DEC_H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+        od = torch.empty_like(vd)
+
+        def dec():
+            _lib.check(L.fakla_decode_mapped(qm.data_ptr(), km.data_ptr(), vd.data_ptr(), None, od.data_ptr(),
+                                             S.data_ptr(), z.data_ptr(), DEC_N, DEC_H, D, D, _lib.FAKLA_BF16, sh))
+        fn = dec
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    ms = time_loop(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+    _lib.check(L.fakla_device_status(sh))
+    print(json.dumps({"only": args.only, "launches": args.warmup + args.steps, "ms_per_launch": ms}), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -241,9 +297,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", choices=["phi", "scan", "decode"],
+                    help="launch just one kernel (warmup + steps launches); for profiler captures")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.only:
+        return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
 
     rank = int(os.environ.get("RANK", "0"))
@@ -363,16 +423,17 @@ def main():
         Wd, bd = lpm_init(DEC_IN, DEC_H * D)
         Wd, bd = Wd.bfloat16().to(dev), bd.bfloat16().to(dev)
         nsteps = DEC_STEPS
-        qd = (torch.randn(nsteps, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
-        kd = (torch.randn(nsteps, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
-        vd = (torch.randn(nsteps, DEC_N, DEC_H, D, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        ring = 16  # distinct token inputs, cycled (the state evolves every step regardless)
+        qd = (torch.randn(ring, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        kd = (torch.randn(ring, DEC_N, DEC_IN, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
+        vd = (torch.randn(ring, DEC_N, DEC_H, D, generator=gd, device=dev) / math.sqrt(D)).bfloat16()
         od = torch.empty(DEC_N, DEC_H, D, device=dev, dtype=torch.bfloat16)
         dws = L.fakla_decode_workspace_bytes(DEC_N, DEC_IN, DEC_H, D, D, _lib.FAKLA_BF16)
         dwsb = torch.empty(dws, device=dev, dtype=torch.uint8)
         it = [0]
 
         def dstep():
-            i = it[0] % nsteps
+            i = it[0] % ring
             it[0] += 1
             _lib.check(L.fakla_decode(qd[i].data_ptr(), kd[i].data_ptr(), vd[i].data_ptr(), None, Wd.data_ptr(),
                                       bd.data_ptr(), od.data_ptr(), Sd.data_ptr(), zd.data_ptr(), DEC_N, DEC_IN,

@@ -57,7 +57,16 @@ def test_library_has_no_unresolved_cuda_runtime_dependency():
     assert "libcudart" not in out
 
 
+def _no_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("dummy-pointer validation checks run only where no GPU exists; "
+                    "the GPU tests cover validation with real buffers")
+
+
 def test_argument_validation_without_device():
+    _no_gpu()
     lib = _lib.lib()
     p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
     # bad dtype
@@ -96,10 +105,7 @@ def test_workspace_queries():
 
 
 def test_call_without_gpu_reports_error_not_crash():
-    import torch
-
-    if torch.cuda.is_available():
-        pytest.skip("this checks the no-GPU path")
+    _no_gpu()
     lib = _lib.lib()
     p = ctypes.c_void_p(16)
     rc = lib.fakla_attention(p, p, p, None, p, None, None, 1, 1, 1, 8, 8, 0, 0, None, 0, None)
