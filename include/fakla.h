@@ -172,6 +172,34 @@ size_t fakla_decode_workspace_bytes(int64_t N, int64_t in_dim, int64_t H,
                                     int64_t M, int64_t Dv, int dtype);
 
 /*
+ * fakla_decode_noalloc -- fakla_decode for callers that cannot allocate
+ * device memory. No counterpart in the reference (it has no decode step and
+ * no C ABI); this is an addition of this library.
+ *
+ * Who needs it: hosts that bind the library through a bare C FFI and have no
+ * device allocator to hand it a workspace, and per-token decode loops where a
+ * cudaMalloc (which synchronises the device and can fail under memory
+ * pressure) is not allowed. Same arguments and results as fakla_decode minus
+ * the workspace: the phi(q), phi(k) scratch lives in a static device array of
+ * FAKLA_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * process exit; nothing is allocated per call.
+ * Limit: 2 * N * H * M * sizeof(element) <= FAKLA_NOALLOC_SCRATCH_BYTES
+ * (e.g. N=256, H=32, M=128 in bf16 uses 4 MiB); larger steps are rejected with
+ * FAKLA_ERR_UNSUPPORTED. The first call on a device looks up the array's
+ * device address; make it before any stream capture. All calls share the one
+ * array: calls whose GPU work overlaps race on it and must be serialised by
+ * the caller. Nothing in it needs to start at zero (each call writes all the
+ * scratch it reads).
+ */
+#define FAKLA_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+int fakla_decode_noalloc(const void* q, const void* k, const void* v,
+                         const void* temp, const void* W, const void* bias,
+                         void* out, float* S, float* z, int64_t N,
+                         int64_t in_dim, int64_t H, int64_t M, int64_t Dv,
+                         int dtype, void* stream);
+
+/*
  * fakla_device_status -- synchronise `stream` and return (then clear) the
  * device-side status word that kernels set when a bounded wait expires
  * (FAKLA_ERR_TIMEOUT) or a device-side check fails. FAKLA_OK if clean.

@@ -48,6 +48,7 @@ SIGNATURES = {
     "fakla_decode_mapped": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
     "fakla_decode": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "fakla_decode_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
+    "fakla_decode_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p]),
     "fakla_device_status": (_int, [_p]),
 }
 

@@ -93,6 +93,12 @@ def test_argument_validation_without_device():
     # decode needs state
     rc = lib.fakla_decode_mapped(p, p, p, None, p, None, None, 1, 1, 8, 8, 0, None)
     assert rc == 1
+    # no-allocation decode: a step whose phi scratch exceeds the static array
+    N, H, M = 1024, 32, 128  # 2*N*H*M*2 B = 16 MiB > 8 MiB
+    rc = lib.fakla_decode_noalloc(p, p, p, None, p, None, p, p, p, N, H * M, H, M, M, 1, None)
+    assert rc == 2 and b"scratch" in lib.fakla_last_error()
+    rc = lib.fakla_decode_noalloc(p, p, p, None, p, None, p, p, p, 0, 1, 1, 1, 1, 1, None)
+    assert rc == 1
 
 
 def test_workspace_queries():
