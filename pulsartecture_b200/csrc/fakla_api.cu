@@ -7,6 +7,7 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -201,7 +202,7 @@ bool use_sm100_phi(int dtype, const void* x0, const void* x1, const void* W, con
                    int64_t heads) {
   return dtype == FAKLA_BF16 && fakla::phi_sm100_supported(rows, K, N, heads) && aligned16(x0) &&
          (x1 == nullptr || aligned16(x1)) && aligned16(W) && aligned16(out0) &&
-         (out1 == nullptr || aligned16(out1)) && (bias == nullptr || ((uintptr_t)bias & 3u) == 0);
+         (out1 == nullptr || aligned16(out1)) && (bias == nullptr || aligned16(bias));
 }
 
 int run_attention(const void* q, const void* k, const void* v, const void* temp, void* out,

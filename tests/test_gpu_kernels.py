@@ -66,6 +66,8 @@ def test_device_status_clean(cuda):
     (1000, 2048, 2048, 16, True, True),
     (1, 256, 512, 2, False, True),
     (130, 4096, 512, 4, True, False),
+    (4096, 2048, 2048, 16, True, True),
+    (5000, 1024, 512, 4, False, True),    # ragged last row tile
 ])
 def test_phi_bf16_tensor_core(cuda, rows, K, N, heads, use_bias, use_temp):
     from pulsartecture_b200.backend.interface import phi_map
