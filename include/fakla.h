@@ -99,6 +99,13 @@ int fakla_attention(const void* q_mapped, const void* k_mapped, const void* v,
                     unsigned flags, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/*
+ * Workspace that lets fakla_attention split long sequences into segments run
+ * by separate CTAs (when B*H alone would leave SMs idle): one fp32 (S, z)
+ * record per segment. 0 when the call would not be split on the current
+ * device. The workspace is optional: with less (or NULL) the scan runs one
+ * CTA per (b, h) sequence, with the same result up to fp32 rounding.
+ */
 size_t fakla_attention_workspace_bytes(int64_t B, int64_t T, int64_t H,
                                        int64_t Df, int64_t Dv, int dtype);
 
@@ -131,7 +138,9 @@ int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
  *          contiguous shard of heads on a multi-GPU run).
  *   v    : (B, T, H, Dv)   temp : (B, T, H) or NULL   out : (B, T, H, Dv)
  *   S, z, flags : as fakla_attention, with Df = M.
- * Needs workspace >= fakla_prefill_workspace_bytes() (holds phi(q), phi(k)).
+ * Workspace: fakla_prefill_workspace_bytes() = phi(q) and phi(k) buffers
+ * (required) followed by the scan's segment records (optional, as in
+ * fakla_attention_workspace_bytes).
  */
 int fakla_prefill(const void* q, const void* k, const void* v, const void* temp,
                   const void* W, const void* bias, void* out, float* S, float* z,

@@ -130,9 +130,13 @@ def fa_kla_attention_with_state(q_mapped: torch.Tensor, k_mapped: torch.Tensor, 
         return out, ((S, z) if return_state else None)
     L = _lib.lib()
     with torch.cuda.device(dev):
+        # segment records of the tensor-core scan (0 bytes unless few (b, h)
+        # pairs would leave SMs idle)
+        ws_bytes = L.fakla_attention_workspace_bytes(B, T, H, Df, Dv, code)
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
         _lib.check(L.fakla_attention(
             _ptr(q_mapped), _ptr(k_mapped), _ptr(v_reshaped), _ptr(temp), _ptr(out), _ptr(S), _ptr(z),
-            B, T, H, Df, Dv, code, flags, None, 0, _stream(dev)))
+            B, T, H, Df, Dv, code, flags, _ptr(ws), ws_bytes, _stream(dev)))
     return out, ((S, z) if return_state else None)
 
 

@@ -172,6 +172,10 @@ constexpr int64_t kMaxHeadDim = 256;
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 inline size_t esize(int dtype) { return dtype == FAKLA_BF16 ? 2 : 4; }
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+// One of the two phi(q) / phi(k) buffers of the prefill workspace.
+inline size_t phi_buffer_bytes(int64_t B, int64_t T, int64_t H, int64_t M, int dtype) {
+  return round_up((size_t)B * (size_t)T * (size_t)H * (size_t)M * esize(dtype), 256);
+}
 
 int check_dtype(int dtype) {
   if (dtype != FAKLA_F32 && dtype != FAKLA_BF16)
@@ -207,11 +211,12 @@ bool use_sm100_phi(int dtype, const void* x0, const void* x1, const void* W, con
 
 int run_attention(const void* q, const void* k, const void* v, const void* temp, void* out,
                   float* S, float* z, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv,
-                  int dtype, unsigned flags, cudaStream_t stream, DeviceInfo* d) {
+                  int dtype, unsigned flags, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream, DeviceInfo* d) {
   if (use_sm100_scan(dtype, q, k, v, out, S, B, T, H, Df, Dv)) {
     bool enc = false;
-    cudaError_t e = fakla::launch_scan_sm100(q, k, v, temp, out, S, z, B, T, H, flags, stream,
-                                             d->status, &enc);
+    cudaError_t e = fakla::launch_scan_sm100(q, k, v, temp, out, S, z, B, T, H, flags, workspace,
+                                             workspace_bytes, d->sms, stream, d->status, &enc);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
     return FAKLA_OK;
@@ -248,17 +253,24 @@ int run_phi(const void* x0, const void* x1, const void* W, const void* bias, con
 // ---------------------------------------------------------------------------
 // Entry points
 // ---------------------------------------------------------------------------
-extern "C" size_t fakla_attention_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t,
-                                                  int) {
-  return 0;
+// Workspace of the segmented tensor-core scan (long sequences, few (b, h)
+// pairs): one (S, z) fp32 record per segment. Zero when the call would not be
+// segmented on the current device.
+static size_t scan_workspace(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv, int dtype) {
+  if (dtype != FAKLA_BF16 || !fakla::scan_sm100_supported(B, T, H, Df, Dv)) return 0;
+  return round_up(fakla::scan_sm100_workspace_bytes(B, T, H, fakla_sm_count()), 256);
+}
+
+extern "C" size_t fakla_attention_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Df,
+                                                  int64_t Dv, int dtype) {
+  if (B < 1 || T < 1 || H < 1 || Df < 1 || Dv < 1) return 0;
+  return scan_workspace(B, T, H, Df, Dv, dtype);
 }
 
 extern "C" int fakla_attention(const void* q, const void* k, const void* v, const void* temp,
                                void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                                int64_t Df, int64_t Dv, int dtype, unsigned flags, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int rc = check_dtype(dtype);
   if (rc) return rc;
   if (!q || !k || !v || !out)
@@ -271,8 +283,8 @@ extern "C" int fakla_attention(const void* q, const void* k, const void* v, cons
   if ((rc = check_state(S, z, flags))) return rc;
   DeviceInfo* d = nullptr;
   if ((rc = require_device(&d))) return rc;
-  return run_attention(q, k, v, temp, out, S, z, B, T, H, Df, Dv, dtype, flags,
-                       (cudaStream_t)stream, d);
+  return run_attention(q, k, v, temp, out, S, z, B, T, H, Df, Dv, dtype, flags, workspace,
+                       workspace_bytes, (cudaStream_t)stream, d);
 }
 
 extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
@@ -295,10 +307,8 @@ extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const v
 extern "C" size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim, int64_t H,
                                                 int64_t M, int64_t Dv, int dtype) {
   (void)in_dim;
-  (void)Dv;
-  if (B < 1 || T < 1 || H < 1 || M < 1) return 0;
-  const size_t one = round_up((size_t)B * (size_t)T * (size_t)H * (size_t)M * esize(dtype), 256);
-  return 2 * one;
+  if (B < 1 || T < 1 || H < 1 || M < 1 || Dv < 1) return 0;
+  return 2 * phi_buffer_bytes(B, T, H, M, dtype) + scan_workspace(B, T, H, M, Dv, dtype);
 }
 
 extern "C" int fakla_prefill(const void* q, const void* k, const void* v, const void* temp,
@@ -315,10 +325,12 @@ extern "C" int fakla_prefill(const void* q, const void* k, const void* v, const 
   if (M > kMaxHeadDim || Dv > kMaxHeadDim)
     return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
   if ((rc = check_state(S, z, flags))) return rc;
-  const size_t need = fakla_prefill_workspace_bytes(B, T, in_dim, H, M, Dv, dtype);
+  // phi(q), phi(k) buffers are required; the scan's segment records (the
+  // rest of fakla_prefill_workspace_bytes) are used when they fit.
+  const size_t need = 2 * phi_buffer_bytes(B, T, H, M, dtype);
   if (workspace == nullptr || workspace_bytes < need)
-    return fakla_set_error(FAKLA_ERR_WORKSPACE, "prefill needs %zu workspace bytes, got %zu", need,
-                           workspace == nullptr ? (size_t)0 : workspace_bytes);
+    return fakla_set_error(FAKLA_ERR_WORKSPACE, "prefill needs at least %zu workspace bytes, got %zu",
+                           need, workspace == nullptr ? (size_t)0 : workspace_bytes);
   if (!aligned16(workspace))
     return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
   DeviceInfo* d = nullptr;
@@ -326,13 +338,16 @@ extern "C" int fakla_prefill(const void* q, const void* k, const void* v, const 
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t rows = B * T;
   uint8_t* ws = (uint8_t*)workspace;
+  const size_t one = phi_buffer_bytes(B, T, H, M, dtype);
   void* phq = ws;
-  void* phk = ws + need / 2;
+  void* phk = ws + one;
   // phi(q) and phi(k)*temp in one launch (k-side temperature fused, so the
-  // scan below runs with temp = NULL).
+  // scan below runs with temp = NULL); the rest of the workspace holds the
+  // scan's segment records.
   rc = run_phi(q, k, W, bias, nullptr, temp, phq, phk, rows, in_dim, H * M, H, dtype, st, d);
   if (rc) return rc;
-  return run_attention(phq, phk, v, nullptr, out, S, z, B, T, H, M, Dv, dtype, flags, st, d);
+  return run_attention(phq, phk, v, nullptr, out, S, z, B, T, H, M, Dv, dtype, flags,
+                       ws + 2 * one, workspace_bytes - 2 * one, st, d);
 }
 
 extern "C" int fakla_decode_mapped(const void* q, const void* k, const void* v, const void* temp,

@@ -34,8 +34,15 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
                              int64_t rows, int64_t K, int64_t N, int64_t heads,
                              cudaStream_t stream, int* status, bool* encoded);
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
+// Segments per sequence the scan uses on a device with `sms` SMs (1 = one CTA
+// per sequence), and the workspace that takes (0 when G = 1).
+int scan_sm100_segments(int64_t B, int64_t T, int64_t H, int sms);
+size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms);
+// Falls back to one CTA per sequence when `workspace` is smaller than
+// scan_sm100_workspace_bytes() (or NULL).
 cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
-                              unsigned flags, cudaStream_t stream, int* status, bool* encoded);
+                              unsigned flags, void* workspace, size_t workspace_bytes, int sms,
+                              cudaStream_t stream, int* status, bool* encoded);
 
 }  // namespace fakla

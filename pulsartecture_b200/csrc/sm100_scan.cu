@@ -1,26 +1,42 @@
 // Chunked causal FA-KLA scan on the sm_100a tensor cores (Df = Dv = 128, bf16
-// activations, fp32 state). One CTA per (b, h) sequence walks its T tokens in
-// chunks of C = 128. For chunk c with rows Q = phi(q), K = phi(k)*temp, V:
+// activations, fp32 state). A CTA walks the tokens of one (b, h) sequence, or
+// of one segment of it, in chunks of C = 128. For chunk c with rows
+// Q = phi(q), K = phi(k)*temp, V:
 //
-//   P   = Q K^T                     (128x128, fp32 in TMEM)        [MMA1]
-//   Pm  = causal_mask_inclusive(P)  (s <= t), split hi+lo bf16 into TMEM
-//   O   = Q S_{<c}                  (S_{<c} as bf16 in smem)       [MMA2]
-//   O  += Pm_hi V + Pm_lo V         (A operand straight from TMEM)  [MMA3]
-//   S  += K^T V                     (fp32 accumulator kept in TMEM) [MMA4]
-//   den = rowsum(Pm) + Q . z_{<c};  z += colsum(K)   (fp32, CUDA cores)
-//   out = O / (den + 1e-12)
+//   P   = Q K^T                      (128x128 fp32, TMEM)            [MMA1]
+//   Pm  = causal_mask_inclusive(P)   split into bf16 hi + lo, in place in TMEM
+//   O   = Q S_{<c}                   (S_{<c} as bf16 in smem)        [MMA2]
+//   Dz  = Q [z_hi z_lo]              (z_{<c} split hi/lo, N = 16)    [MMA2b]
+//   S  += K^T V                      (fp32, lives in TMEM)           [MMA4]
+//   z  += K^T 1                      (fp32, N = 16, column 0)        [MMA4b]
+//   O  += Pm_hi V + Pm_lo V          (A operand straight from TMEM)  [MMA3]
+//   out = O / (rowsum(Pm) + Dz[0] + Dz[1] + 1e-12)
 //
 // This is the chunk-parallel form of the reference recurrence
 // (ultra_rwka/backend/cpp/cpu/cpu_kernels.cpp:107-164): out_t sums k~_s v_s
-// over s <= t, exactly as the per-token loop does, with the state carried
-// across chunks.
+// (and k~_s for the denominator) over s <= t, exactly as the per-token loop
+// does, with the state carried across chunks.
 //
-// Warp roles (192 threads): warp 0 TMA producer (Q, K, V tiles, 2 stages);
-// warp 1 TMEM allocator + MMA issuer; warps 2..5 (128 threads, thread r owns
-// TMEM lane r: token r for P/O, feature r for S) mask/split P, refresh the
-// bf16 copy of S, update z, normalise and store the output.
+// Warp roles (448 threads): warp 0 TMA producer (Q, K, V tiles, 2 stages);
+// warp 1 TMEM allocator + single-thread MMA issuer; three warpgroups, each
+// thread owning one TMEM lane (token r for P/O, feature r for S/z):
+//   warps 2-5   (P)  inclusive mask + hi/lo split of P, row sums; k*temp
+//   warps 6-9   (S)  state refresh: S (TMEM fp32) -> bf16 smem operand,
+//                    z -> hi/lo operand; initial state in, final state out
+//   warps 10-13 (O)  normalise O and store the output rows
+// so the mask of chunk c+1 overlaps the normalisation of chunk c and the
+// state refresh, and the tensor pipe sees MMA2/MMA4 of one chunk between
+// MMA1 and MMA3 of the next.
+//
+// Long sequences with few (b, h) pairs are split into G segments of whole
+// chunks: scan_delta_sm100_kernel sums K^T V and K^T 1 over each segment but
+// the last, scan_prefix_kernel turns those into each segment's initial state
+// (plus the caller's initial state), and the main kernel runs one CTA per
+// (b, h, segment).
+//
 // Every wait is bounded; on expiry the kernel records FAKLA_ERR_TIMEOUT in the
-// device status word and winds down.
+// device status word and winds down (copies and MMAs in flight are drained
+// before TMEM is freed).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -40,19 +56,32 @@ constexpr int D = 128;                       // Df = Dv
 constexpr int kAtom = C * 128;               // 16 KB: 128 rows x 64 bf16
 constexpr int kTile = 2 * kAtom;             // 32 KB: 128 rows x 128 bf16
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 448;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColP = 0, kColO = 128, kColS = 256, kColPh = 384, kColPl = 448;
+// TMEM columns: P (hi/lo written in place), O, S, z accumulator, Q.z result,
+// and the two parity slots of the per-row sum of the masked P.
+constexpr uint32_t kColP = 0, kColO = 128, kColS = 256, kColZ = 384, kColDz = 400, kColRs = 416;
 constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr int64_t kStateFloats = (int64_t)D * D + D;  // one (S, z) record
 
-// smem: Q[2] K[2] V[2] Sb | z[128] f32 | barriers
+// Shared memory. Barriers sit in the first 256 bytes of the dynamic window;
+// the operand region starts at the next 1024-byte boundary:
+//   Q[2] K[2] V[2] (32 KB each) | M0 | M1 | Sb (32 KB)
+// M0/M1 are two 1 KB swizzle atoms holding the N=16 K-major operands:
+//   ZK (z_{<c} as bf16 hi in row 0, lo in row 1; features 0-63 in M0, 64-127
+//   in M1) and ONES (rows 4 and 5 of M0 all 1.0). Only those rows feed result
+//   columns that are read; the other rows of the 16-row operands fall on
+//   whatever lies there (M0/M1/Sb) and only produce columns nobody reads.
 constexpr size_t kOffQ = 0;
 constexpr size_t kOffK = kOffQ + kStages * kTile;
 constexpr size_t kOffV = kOffK + kStages * kTile;
-constexpr size_t kOffSb = kOffV + kStages * kTile;
-constexpr size_t kOffZ = kOffSb + kTile;
-constexpr size_t kOffBar = kOffZ + D * sizeof(float);
-constexpr size_t kSmemBytes = 1024 + kOffBar + 128;
+constexpr size_t kOffM0 = kOffV + kStages * kTile;
+constexpr size_t kOffM1 = kOffM0 + 1024;
+constexpr size_t kOffSb = kOffM1 + 1024;
+constexpr size_t kOperandBytes = kOffSb + kTile;
+constexpr size_t kHeadBytes = 256;
+constexpr size_t kSmemBytes = 1024 + kOperandBytes;  // 232448 = the sm_100 per-CTA maximum
+constexpr uint32_t kSmallSbo = 2048;                 // rows 8-15 of the N=16 operands
 
 enum Bar {
   kFull0 = 0,
@@ -64,16 +93,20 @@ enum Bar {
   kSReady,
   kOFree,
   kKReady,
+  kDrain,
   kNumBars
 };
-static_assert(kNumBars * 8 + 8 <= 128, "barrier area");
+static_assert(kNumBars * 8 + 8 <= kHeadBytes, "barrier area");
 
 struct ScanArgs {
   const __nv_bfloat16* temp;  // (B,T,H) or null
   __nv_bfloat16* out;         // (B,T,H,D)
   float* S;                   // (B,H,D,D) or null
   float* z;                   // (B,H,D) or null
+  const float* seg_init;      // (B*H, G) records of (S, z): each segment's initial state; or null
   int T, H;
+  int G;                      // segments per sequence
+  int seg_chunks;             // chunks per segment
   unsigned flags;
   int* status;
 };
@@ -86,6 +119,15 @@ __device__ __forceinline__ uint64_t mndesc(uint32_t tile_addr, int j) {
   // MN-major operand, K step j: 16 K rows (2048 B) further; MN atoms 16 KB apart.
   return smem_desc_sw128(tile_addr + (uint32_t)(j * 2048), kAtom, 1024);
 }
+// N=16 K-major operands: ZK atoms are the two 1 KB blocks M0, M1; ONES rows
+// 4 and 5 of M0 serve as row 0 of atoms 0 and 1 (a uniform row reads the
+// same under any swizzle phase).
+__device__ __forceinline__ uint64_t zkdesc(uint32_t m0_addr, int j) {
+  return smem_desc_sw128(m0_addr + (uint32_t)((j >> 2) * 1024 + (j & 3) * 32), 16, kSmallSbo);
+}
+__device__ __forceinline__ uint64_t onesdesc(uint32_t m0_addr, int j) {
+  return smem_desc_sw128(m0_addr + 512u + (uint32_t)((j >> 2) * 128 + (j & 3) * 32), 16, kSmallSbo);
+}
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -96,27 +138,119 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
+// k~ = k * temp on row r (one token) of a K tile in shared memory.
+__device__ __forceinline__ void scale_k_row(uint8_t* tK, int r, float tv) {
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint4* p = reinterpret_cast<uint4*>(tK + a * kAtom + r * 128 + ch * 16);
+      uint4 u = *p;
+      float f[8];
+      bf16x8_to_f32(u, f);
+      u = make_uint4(pack_bf16x2(f[0] * tv, f[1] * tv), pack_bf16x2(f[2] * tv, f[3] * tv),
+                     pack_bf16x2(f[4] * tv, f[5] * tv), pack_bf16x2(f[6] * tv, f[7] * tv));
+      *p = u;
+    }
+  }
+}
+
+__device__ __forceinline__ float temp_at(const __nv_bfloat16* temp, int b, int T, int H, int h, int t) {
+  return t < T ? __bfloat162float(temp[((int64_t)b * T + t) * H + h]) : 0.f;
+}
+
+// Write z_f as bf16 hi (row 0) and lo (row 1) of the ZK operand.
+__device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(zf);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(zf - __bfloat162float(hi));
+  uint8_t* blk = m0 + (f >= 64 ? 1024 : 0);
+  *reinterpret_cast<__nv_bfloat16*>(blk + sw128_offset(0, (uint32_t)(f & 63))) = hi;
+  *reinterpret_cast<__nv_bfloat16*>(blk + sw128_offset(1, (uint32_t)(f & 63))) = lo;
+}
+
+// Tokens [sbase, sbase+32) of row r of P (fp32 bits in v): keep s <= r, split
+// each kept value into bf16 hi + lo and store them in place, hi in columns
+// sbase + [0,16) and lo in sbase + [16,32) (two tokens per column). Returns
+// the sum of the kept values.
+__device__ __forceinline__ float mask_split_32(const uint32_t (&v)[32], int sbase, int r,
+                                               uint32_t p_addr) {
+  uint32_t hi[16], lo[16];
+  float rs = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int s0 = sbase + 2 * e;
+    const float x0 = s0 <= r ? __uint_as_float(v[2 * e]) : 0.f;
+    const float x1 = s0 + 1 <= r ? __uint_as_float(v[2 * e + 1]) : 0.f;
+    rs += x0 + x1;
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+    hi[e] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+    lo[e] = pack_bf16x2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+  }
+  tmem_st16(p_addr + (uint32_t)sbase, hi);
+  tmem_st16(p_addr + (uint32_t)(sbase + 16), lo);
+  return rs;
+}
+
+// 32 fp32 values (bits in v) times inv, stored as 32 bf16 at dst (64 bytes).
+__device__ __forceinline__ void store_scaled_32(const uint32_t (&v)[32], float inv,
+                                                __nv_bfloat16* dst) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint4 u;
+    u.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * inv, __uint_as_float(v[8 * g + 1]) * inv);
+    u.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * inv, __uint_as_float(v[8 * g + 3]) * inv);
+    u.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * inv, __uint_as_float(v[8 * g + 5]) * inv);
+    u.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * inv, __uint_as_float(v[8 * g + 7]) * inv);
+    *reinterpret_cast<uint4*>(dst + 8 * g) = u;
+  }
+}
+
+// Warp-uniform forms of the bounded wait and of the abort check, for warps
+// that go on to issue .sync.aligned tcgen05 loads and stores.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitNs));
+}
+__device__ __forceinline__ bool warp_aborted(volatile int* abort_flag) {
+  return __any_sync(0xffffffffu, *abort_flag != 0);
+}
+
+__device__ __forceinline__ uint8_t* operand_base(uint8_t* raw) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + kHeadBytes + 1023) &
+                                    ~uintptr_t(1023));
+}
+
 __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const ScanArgs args) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* smem = operand_base(smem_raw);
+  // The operand region must end inside the allocation (true unless the
+  // dynamic window starts more than 768 bytes past a 1 KB boundary).
+  if (smem + kOperandBytes > smem_raw + kSmemBytes) {
+    if (threadIdx.x == 0) report_status(args.status, FAKLA_ERR_ALIGNMENT);
+    return;
+  }
   uint8_t* sQ = smem + kOffQ;
   uint8_t* sK = smem + kOffK;
   uint8_t* sV = smem + kOffV;
+  uint8_t* sM0 = smem + kOffM0;
   uint8_t* sSb = smem + kOffSb;
-  float* zs = reinterpret_cast<float*>(smem + kOffZ);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x / args.H;
-  const int h = blockIdx.x % args.H;
-  const int nchunks = (args.T + C - 1) / C;
+  const int bh_idx = blockIdx.x / args.G;
+  const int seg = blockIdx.x % args.G;
+  const int b = bh_idx / args.H;
+  const int h = bh_idx % args.H;
+  const int nchunks_total = (args.T + C - 1) / C;
+  const int c0 = seg * args.seg_chunks;
+  const int c1 = min(nchunks_total, c0 + args.seg_chunks);
+  const int nch = c1 - c0;
   const bool has_temp = args.temp != nullptr;
+  const bool last_seg = seg == args.G - 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -130,12 +264,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     mbar_init(&bars[kSReady], 4);
     mbar_init(&bars[kOFree], 4);
     mbar_init(&bars[kKReady], 4);
+    mbar_init(&bars[kDrain], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
+  // ONES: rows 4-5 of M0 (256 bytes of bf16 1.0).
+  if (threadIdx.x < 64)
+    reinterpret_cast<uint32_t*>(sM0 + 512)[threadIdx.x] = 0x3F803F80u;
+  fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -148,9 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      for (int c = 0; c < nchunks && !*abort_flag; ++c) {
-        const int st = c & 1;
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
+      int issued = 0;
+      for (int i = 0; i < nch && !*abort_flag; ++i) {
+        const int st = i & 1;
+        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
         if (!mbar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
@@ -158,213 +298,191 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         }
         uint64_t* fb = &bars[kFull0 + st];
         mbar_arrive_expect_tx(fb, 3 * kTile);
+        const int t0 = (c0 + i) * C;
         for (int a = 0; a < 2; ++a) {
-          tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, c * C, b);
-          tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, c * C, b);
-          tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, c * C, b);
+          tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, t0, b);
+          tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+          tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
         }
+        ++issued;
       }
       if (*abort_flag) {
         // Let this CTA's own copies in flight land before the CTA exits.
-        for (int c = nchunks - 2; c < nchunks; ++c)
-          if (c >= 0) (void)mbar_wait(&bars[kFull0 + (c & 1)], (uint32_t)(c >> 1) & 1u, kWaitNs);
+        for (int i = issued - kStages; i < issued; ++i)
+          if (i >= 0) (void)mbar_wait(&bars[kFull0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       constexpr uint32_t idP = idesc_bf16_f32(128, 128, false, false);   // Q . K^T
-      constexpr uint32_t idOi = idesc_bf16_f32(128, 128, false, true);   // Q . S
-      constexpr uint32_t idOt = idesc_bf16_f32(128, 128, false, true);   // Pm . V
-      constexpr uint32_t idS = idesc_bf16_f32(128, 128, true, true);     // K^T . V
+      constexpr uint32_t idQS = idesc_bf16_f32(128, 128, false, true);   // Q . S
+      constexpr uint32_t idQZ = idesc_bf16_f32(128, 16, false, false);   // Q . [z_hi z_lo]
+      constexpr uint32_t idPV = idesc_bf16_f32(128, 128, false, true);   // Pm . V
+      constexpr uint32_t idKV = idesc_bf16_f32(128, 128, true, true);    // K^T . V
+      constexpr uint32_t idK1 = idesc_bf16_f32(128, 16, true, false);    // K^T . 1
       const uint32_t aSb = smem_u32(sSb);
+      const uint32_t aM0 = smem_u32(sM0);
       bool ok = true;
-      for (int c = 0; c < nchunks && ok && !*abort_flag; ++c) {
-        const int st = c & 1;
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
-        const uint32_t par = (uint32_t)c & 1u, prev = (uint32_t)(c - 1) & 1u;
+      bool issued_any = false;
+      for (int i = 0; i < nch && ok && !*abort_flag; ++i) {
+        const int st = i & 1;
+        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+        const uint32_t par = (uint32_t)i & 1u, prev = (uint32_t)(i - 1) & 1u;
         ok = mbar_wait(&bars[kFull0 + st], ph, kWaitNs);
         if (ok && has_temp) ok = mbar_wait(&bars[kKReady], par, kWaitNs);
-        if (ok && c > 0) ok = mbar_wait(&bars[kE1Done], prev, kWaitNs);
         if (!ok) break;
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + st * kTile);
         const uint32_t aK = smem_u32(sK + st * kTile);
         const uint32_t aV = smem_u32(sV + st * kTile);
-        // MMA1: P = Q K^T
+        issued_any = true;
+        // MMA1: P = Q K^T (overwrites the hi/lo of the previous chunk, which
+        // MMA3 of that chunk, issued earlier, has consumed: MMAs run in order)
 #pragma unroll
         for (int j = 0; j < 8; ++j) mma_ss(tmem + kColP, kdesc(aQ, j), kdesc(aK, j), idP, j > 0);
         mma_commit(&bars[kBarP]);
         ok = mbar_wait(&bars[kSReady], par, kWaitNs);
-        if (ok && c > 0) ok = mbar_wait(&bars[kOFree], prev, kWaitNs);
+        if (ok && i > 0) ok = mbar_wait(&bars[kOFree], prev, kWaitNs);
         if (!ok) break;
         tc_fence_after();
-        // MMA2: O = Q S_{<c}   (B = bf16 S in smem, MN-major: rows f, dv contiguous)
+        // MMA2 / MMA2b: O = Q S_{<c}, Dz = Q [z_hi z_lo]
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColO, kdesc(aQ, j), mndesc(aSb, j), idOi, j > 0);
-        // MMA4: S += K^T V   (A = K as M=f x K=s, MN-major; B = V MN-major)
+        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColO, kdesc(aQ, j), mndesc(aSb, j), idQS, j > 0);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColS, mndesc(aK, j), mndesc(aV, j), idS, 1u);
+        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColDz, kdesc(aQ, j), zkdesc(aM0, j), idQZ, j > 0);
+        // MMA4 / MMA4b: S += K^T V, z += K^T 1 (A = K as M=f x K=s, MN-major)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColS, mndesc(aK, j), mndesc(aV, j), idKV, 1u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColZ, mndesc(aK, j), onesdesc(aM0, j), idK1, 1u);
         mma_commit(&bars[kBarS]);
         ok = mbar_wait(&bars[kE1Done], par, kWaitNs);
         if (!ok) break;
         tc_fence_after();
-        // MMA3: O += Pm_hi V + Pm_lo V   (A from TMEM: 16 bf16 = 8 columns per K step)
+        // MMA3: O += Pm_hi V + Pm_lo V. Hi/lo of tokens [32g, 32g+32) sit in
+        // columns 32g + [0,16) and 32g + [16,32); K step j = 16 tokens.
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          mma_ts(tmem + kColO, tmem + kColPh + (uint32_t)(8 * j), mndesc(aV, j), idOt, 1u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          mma_ts(tmem + kColO, tmem + kColPl + (uint32_t)(8 * j), mndesc(aV, j), idOt, 1u);
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t col = kColP + (uint32_t)(32 * (j >> 1) + 8 * (j & 1));
+          mma_ts(tmem + kColO, tmem + col, mndesc(aV, j), idPV, 1u);
+          mma_ts(tmem + kColO, tmem + col + 16u, mndesc(aV, j), idPV, 1u);
+        }
         mma_commit(&bars[kBarO]);
         mma_commit(&bars[kEmpty0 + st]);
       }
       if (!ok) {
         report_status(args.status, FAKLA_ERR_TIMEOUT);
         *abort_flag = 1;
+        if (issued_any) {
+          // Drain the MMAs in flight before TMEM and smem are released.
+          mma_commit(&bars[kDrain]);
+          (void)mbar_wait(&bars[kDrain], 0, kWaitNs);
+        }
       }
     }
-  } else {
-    // ---------------------------------------------------------------- compute
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- P: mask + split
     const int q4 = warp & 3;
-    const int r = 32 * q4 + lane;  // TMEM lane: token r (P, O) / feature r (S)
+    const int r = 32 * q4 + lane;  // token r of the chunk
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+    bool ok = true;
+    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+      const uint32_t par = (uint32_t)i & 1u;
+      if (has_temp) {
+        const int st = i & 1;
+        ok = warp_wait(&bars[kFull0 + st], (uint32_t)(i >> 1) & 1u);
+        if (!ok) break;
+        scale_k_row(sK + st * kTile, r, temp_at(args.temp, b, args.T, args.H, h, (c0 + i) * C + r));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kKReady]);
+      }
+      ok = warp_wait(&bars[kBarP], par);
+      if (!ok) break;
+      tc_fence_after();
+      float rs = 0.f;
+#pragma unroll 1
+      for (int g2 = 0; g2 < 2; ++g2) {
+        uint32_t va[32], vb[32];
+        tmem_ld32(lane_addr + kColP + (uint32_t)(64 * g2), va);
+        tmem_ld32(lane_addr + kColP + (uint32_t)(64 * g2 + 32), vb);
+        tmem_ld_wait();
+        rs += mask_split_32(va, 64 * g2, r, lane_addr + kColP);
+        rs += mask_split_32(vb, 64 * g2 + 32, r, lane_addr + kColP);
+      }
+      tmem_st1(lane_addr + kColRs + par, __float_as_uint(rs));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kE1Done]);
+    }
+    if (!ok) {
+      report_status(args.status, FAKLA_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else if (warp < 10) {
+    // ---------------------------------------------------------------- S: state refresh
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;  // feature r
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     const int64_t bh = (int64_t)b * args.H + h;
-
-    // ---- initial state: S into TMEM (fp32) and smem (bf16), z into smem
     {
-      const bool load = (args.flags & FAKLA_STATE_IN) && args.S != nullptr;
-      const float* srow = load ? args.S + (bh * D + r) * D : nullptr;
+      // initial state: the segment's record, else the caller's state, else 0
+      const float* srow = nullptr;
+      float z0 = 0.f;
+      if (args.seg_init != nullptr) {
+        const float* rec = args.seg_init + (bh * args.G + seg) * kStateFloats;
+        srow = rec + (int64_t)r * D;
+        z0 = rec[(int64_t)D * D + r];
+      } else if ((args.flags & FAKLA_STATE_IN) && args.S != nullptr) {
+        srow = args.S + (bh * D + r) * D;
+        z0 = args.z[bh * D + r];
+      }
 #pragma unroll 1
       for (int cc = 0; cc < D; cc += 16) {
         uint32_t v[16];
         float f[16];
+        if (srow != nullptr) {
+          const float4* s4 = reinterpret_cast<const float4*>(srow + cc);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          f[i] = load ? srow[cc + i] : 0.f;
-          v[i] = __float_as_uint(f[i]);
+          for (int g = 0; g < 4; ++g) {
+            const float4 x = s4[g];
+            f[4 * g] = x.x;
+            f[4 * g + 1] = x.y;
+            f[4 * g + 2] = x.z;
+            f[4 * g + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = 0.f;
         }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(f[e]);
         tmem_st16(lane_addr + kColS + (uint32_t)cc, v);
         uint32_t p[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) p[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
+        for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(f[2 * e], f[2 * e + 1]);
         uint8_t* atom = sSb + (cc >= 64 ? kAtom : 0);
         const int col = cc & 63;
         *reinterpret_cast<uint4*>(atom + sw128_offset(r, col)) = make_uint4(p[0], p[1], p[2], p[3]);
         *reinterpret_cast<uint4*>(atom + sw128_offset(r, col + 8)) = make_uint4(p[4], p[5], p[6], p[7]);
       }
-      zs[r] = load ? args.z[bh * D + r] : 0.f;
+      tmem_st1(lane_addr + kColZ, __float_as_uint(z0));
+      put_zk(sM0, r, z0);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSReady]);
     }
-
+    const bool write_state = last_seg && (args.flags & FAKLA_STATE_OUT) && args.S != nullptr;
     bool ok = true;
-    for (int c = 0; c < nchunks && !*abort_flag; ++c) {
-      const int st = c & 1;
-      const uint32_t ph = (uint32_t)(c >> 1) & 1u;
-      const uint32_t par = (uint32_t)c & 1u;
-      uint8_t* tQ = sQ + st * kTile;
-      uint8_t* tK = sK + st * kTile;
-      const int t_glob = c * C + r;
-      const bool t_valid = t_glob < args.T;
-
-      ok = mbar_wait(&bars[kFull0 + st], ph, kWaitNs);
-      if (!ok) break;
-      named_barrier_sync(1, 128);  // z of the previous chunk complete everywhere
-
-      if (has_temp) {
-        // k~ = k * temp: scale row r (token) of the K tile in place
-        const float tv = t_valid
-                             ? __bfloat162float(args.temp[((int64_t)b * args.T + t_glob) * args.H + h])
-                             : 0.f;
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            uint4* p = reinterpret_cast<uint4*>(tK + a * kAtom + r * 128 + ch * 16);
-            uint4 u = *p;
-            float f[8];
-            bf16x8_to_f32(u, f);
-            u = make_uint4(pack_bf16x2(f[0] * tv, f[1] * tv), pack_bf16x2(f[2] * tv, f[3] * tv),
-                           pack_bf16x2(f[4] * tv, f[5] * tv), pack_bf16x2(f[6] * tv, f[7] * tv));
-            *p = u;
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kKReady]);
-        named_barrier_sync(1, 128);
-      }
-
-      // den_inter = q_t . z_{<c}   (row r of Q; chunks are position-permuted
-      // inside a row by the swizzle, so read physical chunk p = logical p^(r&7))
-      float dinter = 0.f;
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const uint4 u = *reinterpret_cast<const uint4*>(tQ + a * kAtom + r * 128 + p * 16);
-          const int lc = p ^ (r & 7);
-          float f[8];
-          bf16x8_to_f32(u, f);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dinter = fmaf(f[i], zs[a * 64 + lc * 8 + i], dinter);
-        }
-      }
-      named_barrier_sync(1, 128);  // all reads of z_{<c} done
-      {
-        // z += colsum(K): feature r, all 128 tokens of the chunk
-        const int a = r >> 6, col = r & 63;
-        const uint8_t* base = tK + a * kAtom;
-        float zsum = 0.f;
-#pragma unroll 8
-        for (int s = 0; s < C; ++s) {
-          const __nv_bfloat16 x =
-              *reinterpret_cast<const __nv_bfloat16*>(base + sw128_offset((uint32_t)s, (uint32_t)col));
-          zsum += __bfloat162float(x);
-        }
-        zs[r] += zsum;
-      }
-
-      // ---- E1: P row r -> inclusive causal mask -> hi/lo bf16 into TMEM
-      ok = mbar_wait(&bars[kBarP], par, kWaitNs);
+    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+      ok = warp_wait(&bars[kBarS], (uint32_t)i & 1u);
       if (!ok) break;
       tc_fence_after();
-      float dintra = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < C; cc += 32) {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + kColP + (uint32_t)cc, v);
-        tmem_ld_wait();
-        uint32_t hi[16], lo[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int s0 = cc + 2 * i;
-          float x0 = s0 <= r ? __uint_as_float(v[2 * i]) : 0.f;
-          float x1 = s0 + 1 <= r ? __uint_as_float(v[2 * i + 1]) : 0.f;
-          dintra += x0 + x1;
-          const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-          const float l0 = x0 - __bfloat162float(h0), l1 = x1 - __bfloat162float(h1);
-          hi[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-          lo[i] = pack_bf16x2(l0, l1);
-        }
-        tmem_st16(lane_addr + kColPh + (uint32_t)(cc / 2), hi);
-        tmem_st16(lane_addr + kColPl + (uint32_t)(cc / 2), lo);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kE1Done]);
-
-      // ---- E2: S row r (fp32, TMEM) -> bf16 copy in smem (+ final state out)
-      ok = mbar_wait(&bars[kBarS], par, kWaitNs);
-      if (!ok) break;
-      tc_fence_after();
-      const bool last = (c == nchunks - 1);
-      const bool sout = last && (args.flags & FAKLA_STATE_OUT) && args.S != nullptr;
+      const bool sout = write_state && i == nch - 1;
 #pragma unroll 1
       for (int cc = 0; cc < D; cc += 32) {
         uint32_t v[32];
@@ -372,8 +490,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         tmem_ld_wait();
         uint32_t p[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          p[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        for (int e = 0; e < 16; ++e)
+          p[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
         uint8_t* atom = sSb + (cc >= 64 ? kAtom : 0);
         const int col = cc & 63;
 #pragma unroll
@@ -388,32 +506,50 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
                                  __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
         }
       }
+      uint32_t zraw;
+      tmem_ld1(lane_addr + kColZ, zraw);
+      tmem_ld_wait();
+      const float zf = __uint_as_float(zraw);
+      put_zk(sM0, r, zf);
+      if (sout) args.z[bh * D + r] = zf;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSReady]);
-
-      // ---- E3: out row r = O / (den + eps)
-      ok = mbar_wait(&bars[kBarO], par, kWaitNs);
+    }
+    if (!ok) {
+      report_status(args.status, FAKLA_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  } else {
+    // ---------------------------------------------------------------- O: normalise + store
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;  // token r of the chunk
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+    bool ok = true;
+    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+      const uint32_t par = (uint32_t)i & 1u;
+      ok = warp_wait(&bars[kBarO], par);
       if (!ok) break;
       tc_fence_after();
-      const float inv = 1.f / (dintra + dinter + kEps);
+      uint32_t dz0, dz1, rsr;
+      tmem_ld2(lane_addr + kColDz, dz0, dz1);
+      tmem_ld1(lane_addr + kColRs + par, rsr);
+      tmem_ld_wait();
+      const float inv =
+          1.f / (__uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps);
+      const int t_glob = (c0 + i) * C + r;
+      const bool t_valid = t_glob < args.T;
       __nv_bfloat16* orow = args.out + (((int64_t)b * args.T + t_glob) * args.H + h) * D;
 #pragma unroll 1
-      for (int cc = 0; cc < D; cc += 32) {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + kColO + (uint32_t)cc, v);
+      for (int cc = 0; cc < D; cc += 64) {
+        uint32_t va[32], vb[32];
+        tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
+        tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
         tmem_ld_wait();
         if (t_valid) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * inv, __uint_as_float(v[8 * g + 1]) * inv);
-            u.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * inv, __uint_as_float(v[8 * g + 3]) * inv);
-            u.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * inv, __uint_as_float(v[8 * g + 5]) * inv);
-            u.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * inv, __uint_as_float(v[8 * g + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + cc + 8 * g) = u;
-          }
+          store_scaled_32(va, inv, orow + cc);
+          store_scaled_32(vb, inv, orow + cc + 32);
         }
       }
       tc_fence_before();
@@ -424,7 +560,6 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       report_status(args.status, FAKLA_ERR_TIMEOUT);
       *abort_flag = 1;
     }
-    if (ok && (args.flags & FAKLA_STATE_OUT) && args.z != nullptr) args.z[bh * D + r] = zs[r];
   }
 
   tc_fence_before();
@@ -432,6 +567,232 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Segment sums: for segment g < G-1 of sequence (b, h), dS = sum K~^T V and
+// dz = sum K~ over its chunks, written to record g+1 of the sequence.
+// ---------------------------------------------------------------------------
+constexpr int kDStages = 3;
+constexpr int kDThreads = 192;
+constexpr int kDTile = 2 * kTile;  // K and V of one chunk: 64 KB
+constexpr size_t kDOffOnes = 0;    // 1 KB block, rows 0-1 all 1.0
+constexpr size_t kDOffStages = 1024;
+constexpr size_t kDOperandBytes = kDOffStages + kDStages * kDTile;
+constexpr size_t kDSmemBytes = kHeadBytes + 1024 + kDOperandBytes;
+
+// One k*temp barrier per stage: the scaling warps may run up to three chunks
+// ahead of the MMA warp, more than one barrier's two-phase parity can tell.
+enum DBar {
+  kDFull0 = 0,
+  kDEmpty0 = kDFull0 + kDStages,
+  kDKReady0 = kDEmpty0 + kDStages,
+  kDDone = kDKReady0 + kDStages,
+  kDNumBars
+};
+static_assert(kDNumBars * 8 + 8 <= kHeadBytes, "barrier area");
+
+struct DeltaArgs {
+  const __nv_bfloat16* temp;
+  float* seg_init;  // (B*H, G) records
+  int T, H, G, seg_chunks;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    const DeltaArgs args) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* smem = operand_base(smem_raw);
+  if (smem + kDOperandBytes > smem_raw + kDSmemBytes) {
+    if (threadIdx.x == 0) report_status(args.status, FAKLA_ERR_ALIGNMENT);
+    return;
+  }
+  uint8_t* sOnes = smem + kDOffOnes;
+  uint8_t* sSt = smem + kDOffStages;  // stage s: K at s*kDTile, V at s*kDTile + kTile
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int per = args.G - 1;
+  const int bh_idx = blockIdx.x / per;
+  const int seg = blockIdx.x % per;
+  const int b = bh_idx / args.H;
+  const int h = bh_idx % args.H;
+  const int c0 = seg * args.seg_chunks;
+  const int nch = args.seg_chunks;  // segments before the last are full
+  const bool has_temp = args.temp != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDStages; ++s) {
+      mbar_init(&bars[kDFull0 + s], 1);
+      mbar_init(&bars[kDEmpty0 + s], 1);
+      mbar_init(&bars[kDKReady0 + s], 4);
+    }
+    mbar_init(&bars[kDDone], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (threadIdx.x < 64) reinterpret_cast<uint32_t*>(sOnes)[threadIdx.x] = 0x3F803F80u;
+  fence_proxy_async_smem();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t kDColS = 0, kDColZ = 128;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nch && !*abort_flag; ++i) {
+        const int st = i % kDStages;
+        const uint32_t ph = (uint32_t)(i / kDStages) & 1u;
+        if (!mbar_wait(&bars[kDEmpty0 + st], ph ^ 1u, kWaitNs)) {
+          report_status(args.status, FAKLA_ERR_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        uint64_t* fb = &bars[kDFull0 + st];
+        mbar_arrive_expect_tx(fb, 2 * kTile);
+        const int t0 = (c0 + i) * C;
+        uint8_t* tk = sSt + st * kDTile;
+        for (int a = 0; a < 2; ++a) {
+          tma_load_4d(tk + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+          tma_load_4d(tk + kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
+        }
+        ++issued;
+      }
+      if (*abort_flag) {
+        for (int i = issued - kDStages; i < issued; ++i)
+          if (i >= 0)
+            (void)mbar_wait(&bars[kDFull0 + i % kDStages], (uint32_t)(i / kDStages) & 1u, kWaitNs);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idKV = idesc_bf16_f32(128, 128, true, true);
+      constexpr uint32_t idK1 = idesc_bf16_f32(128, 16, true, false);
+      const uint32_t aOnes = smem_u32(sOnes);
+      bool ok = true;
+      bool issued_any = false;
+      for (int i = 0; i < nch && ok && !*abort_flag; ++i) {
+        const int st = i % kDStages;
+        const uint32_t ph = (uint32_t)(i / kDStages) & 1u;
+        ok = mbar_wait(&bars[kDFull0 + st], ph, kWaitNs);
+        if (ok && has_temp) ok = mbar_wait(&bars[kDKReady0 + st], ph, kWaitNs);
+        if (!ok) break;
+        tc_fence_after();
+        issued_any = true;
+        const uint32_t aK = smem_u32(sSt + st * kDTile);
+        const uint32_t aV = aK + kTile;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          mma_ss(tmem + kDColS, mndesc(aK, j), mndesc(aV, j), idKV, (i > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          // ONES: rows 0 and 1 of the block are row 0 of atoms 0 and 1.
+          const uint64_t ones = smem_desc_sw128(aOnes + (uint32_t)((j >> 2) * 128 + (j & 3) * 32), 16, 1024);
+          mma_ss(tmem + kDColZ, mndesc(aK, j), ones, idK1, (i > 0 || j > 0) ? 1u : 0u);
+        }
+        mma_commit(&bars[kDEmpty0 + st]);
+      }
+      if (!ok) {
+        report_status(args.status, FAKLA_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // Completion of everything issued (also the drain on the error path).
+      if (issued_any) mma_commit(&bars[kDDone]);
+      else mbar_arrive(&bars[kDDone]);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+    bool ok = true;
+    if (has_temp) {
+      for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+        const int st = i % kDStages;
+        ok = warp_wait(&bars[kDFull0 + st], (uint32_t)(i / kDStages) & 1u);
+        if (!ok) break;
+        scale_k_row(sSt + st * kDTile, r, temp_at(args.temp, b, args.T, args.H, h, (c0 + i) * C + r));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kDKReady0 + st]);
+      }
+    }
+    if (ok) ok = warp_wait(&bars[kDDone], 0);
+    if (ok && !warp_aborted(abort_flag)) {
+      tc_fence_after();
+      const int64_t bh = (int64_t)b * args.H + h;
+      float* rec = args.seg_init + (bh * args.G + seg + 1) * kStateFloats;
+      float* srow = rec + (int64_t)r * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D; cc += 32) {
+        uint32_t v[32];
+        tmem_ld32(lane_addr + kDColS + (uint32_t)cc, v);
+        tmem_ld_wait();
+        float4* dst = reinterpret_cast<float4*>(srow + cc);
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                               __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+      }
+      uint32_t zraw;
+      tmem_ld1(lane_addr + kDColZ, zraw);
+      tmem_ld_wait();
+      rec[(int64_t)D * D + r] = __uint_as_float(zraw);
+    }
+    if (!ok) {
+      report_status(args.status, FAKLA_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// Record 0 of each sequence <- the caller's initial state (or 0); record g <-
+// record g-1 + the segment sum stored in record g. One thread per float4 of
+// a record, sequential over the G records (coalesced across threads).
+__global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const float* z_in, int G,
+                                   int state_in) {
+  constexpr int kS4 = D * D / 4;
+  constexpr int kRec4 = (int)(kStateFloats / 4);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kRec4) return;
+  const int64_t bh = blockIdx.y;
+  float4* rec = reinterpret_cast<float4*>(seg_init + bh * G * kStateFloats);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (state_in) {
+    if (i < kS4) {
+      acc = reinterpret_cast<const float4*>(S_in + bh * D * D)[i];
+    } else {
+      const float* zp = z_in + bh * D + 4 * (i - kS4);
+      acc = make_float4(zp[0], zp[1], zp[2], zp[3]);
+    }
+  }
+  rec[i] = acc;
+  for (int g = 1; g < G; ++g) {
+    const float4 d = rec[(int64_t)g * kRec4 + i];
+    acc.x += d.x;
+    acc.y += d.y;
+    acc.z += d.z;
+    acc.w += d.w;
+    rec[(int64_t)g * kRec4 + i] = acc;
   }
 }
 
@@ -452,32 +813,84 @@ static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t
 }
 
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
-  return Df == D && Dv == D && B >= 1 && T >= 1 && H >= 1 && B * H <= (int64_t)INT32_MAX &&
+  return Df == D && Dv == D && B >= 1 && T >= 1 && H >= 1 && B * H <= (int64_t)(INT32_MAX / 256) &&
          T <= (int64_t)INT32_MAX - C;
+}
+
+int scan_sm100_segments(int64_t B, int64_t T, int64_t H, int sms) {
+  const int64_t bh = B * H;
+  const int64_t nchunks = (T + C - 1) / C;
+  if (bh * 4 >= (int64_t)sms * 3) return 1;  // three quarters of the SMs busy already
+  int64_t G = sms / bh;
+  if (G > nchunks / 2) G = nchunks / 2;  // segments of at least two chunks
+  if (G < 2) return 1;
+  const int64_t seg = (nchunks + G - 1) / G;
+  return (int)((nchunks + seg - 1) / seg);
+}
+
+size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
+  const int G = scan_sm100_segments(B, T, H, sms);
+  if (G <= 1) return 0;
+  return (size_t)(B * H) * (size_t)G * (size_t)kStateFloats * sizeof(float);
 }
 
 cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
-                              unsigned flags, cudaStream_t stream, int* status, bool* encoded) {
+                              unsigned flags, void* workspace, size_t workspace_bytes, int sms,
+                              cudaStream_t stream, int* status, bool* encoded) {
   CUtensorMap mQ, mK, mV;
   const bool ok = make_map_bthd(&mQ, q, B, T, H) && make_map_bthd(&mK, k, B, T, H) &&
                   make_map_bthd(&mV, v, B, T, H);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
+  const int64_t nchunks = (T + C - 1) / C;
+  int G = scan_sm100_segments(B, T, H, sms);
+  const size_t need = scan_sm100_workspace_bytes(B, T, H, sms);
+  // Without room for the segment records the scan runs one CTA per sequence.
+  if (G > 1 && (workspace == nullptr || workspace_bytes < need ||
+                (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0))
+    G = 1;
+  const int seg_chunks = (int)((nchunks + G - 1) / G);
+  float* seg_init = G > 1 ? static_cast<float*>(workspace) : nullptr;
+  const bool state_in = (flags & FAKLA_STATE_IN) && S != nullptr;
+
+  if (G > 1) {
+    DeltaArgs d;
+    d.temp = (const __nv_bfloat16*)temp;
+    d.seg_init = seg_init;
+    d.T = (int)T;
+    d.H = (int)H;
+    d.G = G;
+    d.seg_chunks = seg_chunks;
+    d.status = status;
+    cudaError_t e = cudaFuncSetAttribute(scan_delta_sm100_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kDSmemBytes);
+    if (e != cudaSuccess) return e;
+    scan_delta_sm100_kernel<<<(unsigned)(B * H * (G - 1)), kDThreads, kDSmemBytes, stream>>>(mK, mV, d);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const dim3 pgrid((unsigned)((kStateFloats / 4 + 255) / 256), (unsigned)(B * H));
+    scan_prefix_kernel<<<pgrid, 256, 0, stream>>>(seg_init, S, z, G, state_in ? 1 : 0);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+
   ScanArgs a;
   a.temp = (const __nv_bfloat16*)temp;
   a.out = (__nv_bfloat16*)out;
   a.S = S;
   a.z = z;
+  a.seg_init = seg_init;
   a.T = (int)T;
   a.H = (int)H;
+  a.G = G;
+  a.seg_chunks = seg_chunks;
   a.flags = flags;
   a.status = status;
   cudaError_t e = cudaFuncSetAttribute(scan_sm100_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  scan_sm100_kernel<<<(unsigned)(B * H), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, a);
+  scan_sm100_kernel<<<(unsigned)(B * H * G), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, a);
   return cudaGetLastError();
 }
 

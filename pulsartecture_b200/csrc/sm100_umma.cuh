@@ -254,6 +254,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+// 32 lanes x 32 bits, 2 consecutive columns.
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(taddr));
+}
+
+// 32 lanes x 32 bits, one column.
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r0) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r0) : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r0) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r0)
+               : "memory");
+}
+
 // 32 lanes x 32 bits, 16 consecutive columns written from registers.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
