@@ -23,7 +23,9 @@
 //   warps 2-5   (P)  inclusive mask + hi/lo split of P, row sums; k*temp
 //   warps 6-9   (S)  state refresh: S (TMEM fp32) -> bf16 smem operand,
 //                    z -> hi/lo operand; initial state in, final state out
-//   warps 10-13 (O)  normalise O and store the output rows
+//   warps 10-13 (O)  normalise O into the chunk's Q tile (dead by then) and
+//                    TMA-store it; the Q half of a stage is released after
+//                    that store has read it, the K/V half after MMA3
 // so the mask of chunk c+1 overlaps the normalisation of chunk c and the
 // state refresh, and the tensor pipe sees MMA2/MMA4 of one chunk between
 // MMA1 and MMA3 of the next.
@@ -85,8 +87,9 @@ constexpr uint32_t kSmallSbo = 2048;                 // rows 8-15 of the N=16 op
 
 enum Bar {
   kFull0 = 0,
-  kEmpty0 = kFull0 + kStages,
-  kBarP = kEmpty0 + kStages,
+  kEmpty0 = kFull0 + kStages,   // K, V tiles of a stage free (MMA3 done)
+  kEmptyQ0 = kEmpty0 + kStages, // Q tile of a stage free (output stored from it)
+  kBarP = kEmptyQ0 + kStages,
   kBarS,
   kBarO,
   kE1Done,
@@ -100,7 +103,6 @@ static_assert(kNumBars * 8 + 8 <= kHeadBytes, "barrier area");
 
 struct ScanArgs {
   const __nv_bfloat16* temp;  // (B,T,H) or null
-  __nv_bfloat16* out;         // (B,T,H,D)
   float* S;                   // (B,H,D,D) or null
   float* z;                   // (B,H,D) or null
   const float* seg_init;      // (B*H, G) records of (S, z): each segment's initial state; or null
@@ -168,32 +170,56 @@ __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
   *reinterpret_cast<__nv_bfloat16*>(blk + sw128_offset(1, (uint32_t)(f & 63))) = lo;
 }
 
-// Tokens [sbase, sbase+32) of row r of P (fp32 bits in v): keep s <= r, split
-// each kept value into bf16 hi + lo and store them in place, hi in columns
-// sbase + [0,16) and lo in sbase + [16,32) (two tokens per column). Returns
-// the sum of the kept values.
-__device__ __forceinline__ float mask_split_32(const uint32_t (&v)[32], int sbase, int r,
-                                               uint32_t p_addr) {
+// Tokens [sbase, sbase+32) of row r of P (fp32 bits in v), split into bf16
+// hi + lo and stored in place: hi in columns sbase + [0,16), lo in sbase +
+// [16,32) (two tokens per column). kMask keeps only s <= r (the 32-token group
+// on the diagonal); groups below it are kept whole. Returns the sum of the
+// kept values.
+template <bool kMask>
+__device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase, int r,
+                                             uint32_t p_addr) {
   uint32_t hi[16], lo[16];
   float rs = 0.f;
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    const int s0 = sbase + 2 * e;
-    const float x0 = s0 <= r ? __uint_as_float(v[2 * e]) : 0.f;
-    const float x1 = s0 + 1 <= r ? __uint_as_float(v[2 * e + 1]) : 0.f;
+    float x0 = __uint_as_float(v[2 * e]), x1 = __uint_as_float(v[2 * e + 1]);
+    if (kMask) {
+      x0 = sbase + 2 * e <= r ? x0 : 0.f;
+      x1 = sbase + 2 * e + 1 <= r ? x1 : 0.f;
+    }
     rs += x0 + x1;
-    const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-    hi[e] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-    lo[e] = pack_bf16x2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+    const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h2);
+    const __nv_bfloat162 l2 = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+    lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
   }
   tmem_st16(p_addr + (uint32_t)sbase, hi);
   tmem_st16(p_addr + (uint32_t)(sbase + 16), lo);
   return rs;
 }
 
-// 32 fp32 values (bits in v) times inv, stored as 32 bf16 at dst (64 bytes).
-__device__ __forceinline__ void store_scaled_32(const uint32_t (&v)[32], float inv,
-                                                __nv_bfloat16* dst) {
+// Row r of P, token group g (32 tokens) of a warp whose rows are the group
+// q4: below the diagonal (g < q4) kept whole, on it (g == q4) masked.
+__device__ __forceinline__ float split_group_at(const uint32_t (&v)[32], int g, int q4, int r,
+                                                uint32_t p_addr) {
+  return g == q4 ? split_group<true>(v, 32 * g, r, p_addr) : split_group<false>(v, 32 * g, r, p_addr);
+}
+
+// Above the diagonal the whole group is masked: hi = lo = 0.
+__device__ __forceinline__ void zero_group(int g, uint32_t p_addr) {
+  uint32_t zz[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) zz[e] = 0u;
+  tmem_st16(p_addr + (uint32_t)(32 * g), zz);
+  tmem_st16(p_addr + (uint32_t)(32 * g + 16), zz);
+}
+
+// 32 fp32 values (bits in v) times inv, written as bf16 into row r, columns
+// [col0, col0+32) of a 128-row x 128-column 128B-swizzled staging tile.
+__device__ __forceinline__ void stage_scaled_32(const uint32_t (&v)[32], float inv, uint8_t* tile,
+                                                int r, int col0) {
+  uint8_t* atom = tile + (col0 >= 64 ? kAtom : 0);
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     uint4 u;
@@ -201,7 +227,7 @@ __device__ __forceinline__ void store_scaled_32(const uint32_t (&v)[32], float i
     u.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * inv, __uint_as_float(v[8 * g + 3]) * inv);
     u.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * inv, __uint_as_float(v[8 * g + 5]) * inv);
     u.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * inv, __uint_as_float(v[8 * g + 7]) * inv);
-    *reinterpret_cast<uint4*>(dst + 8 * g) = u;
+    *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((col0 & 63) + 8 * g))) = u;
   }
 }
 
@@ -221,7 +247,8 @@ __device__ __forceinline__ uint8_t* operand_base(uint8_t* raw) {
 
 __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmV, const ScanArgs args) {
+    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+    const ScanArgs args) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -256,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kFull0 + s], 1);
       mbar_init(&bars[kEmpty0 + s], 1);
+      mbar_init(&bars[kEmptyQ0 + s], 4);
     }
     mbar_init(&bars[kBarP], 1);
     mbar_init(&bars[kBarS], 1);
@@ -270,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   // ONES: rows 4-5 of M0 (256 bytes of bf16 1.0).
   if (threadIdx.x < 64)
@@ -300,11 +329,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         mbar_arrive_expect_tx(fb, 3 * kTile);
         const int t0 = (c0 + i) * C;
         for (int a = 0; a < 2; ++a) {
-          tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, t0, b);
           tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
           tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
         }
         ++issued;
+        // The Q tile doubles as the output staging of chunk i-2: wait for
+        // that store to have read it.
+        if (!mbar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
+          report_status(args.status, FAKLA_ERR_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        for (int a = 0; a < 2; ++a)
+          tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, t0, b);
       }
       if (*abort_flag) {
         // Let this CTA's own copies in flight land before the CTA exits.
@@ -401,15 +438,26 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       ok = warp_wait(&bars[kBarP], par);
       if (!ok) break;
       tc_fence_after();
+      // Token groups of 32: this warp's rows are group q4, so group g is
+      // whole (g < q4), diagonal (g == q4) or empty (g > q4) for every lane.
+      const uint32_t p_addr = lane_addr + kColP;
       float rs = 0.f;
 #pragma unroll 1
-      for (int g2 = 0; g2 < 2; ++g2) {
+      for (int g0 = 0; g0 < 4; g0 += 2) {
+        if (g0 > q4) {
+          zero_group(g0, p_addr);
+          zero_group(g0 + 1, p_addr);
+          continue;
+        }
         uint32_t va[32], vb[32];
-        tmem_ld32(lane_addr + kColP + (uint32_t)(64 * g2), va);
-        tmem_ld32(lane_addr + kColP + (uint32_t)(64 * g2 + 32), vb);
+        tmem_ld32(p_addr + (uint32_t)(32 * g0), va);
+        if (g0 + 1 <= q4) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
         tmem_ld_wait();
-        rs += mask_split_32(va, 64 * g2, r, lane_addr + kColP);
-        rs += mask_split_32(vb, 64 * g2 + 32, r, lane_addr + kColP);
+        rs += split_group_at(va, g0, q4, r, p_addr);
+        if (g0 + 1 <= q4)
+          rs += split_group_at(vb, g0 + 1, q4, r, p_addr);
+        else
+          zero_group(g0 + 1, p_addr);
       }
       tmem_st1(lane_addr + kColRs + par, __float_as_uint(rs));
       tmem_st_wait();
@@ -538,24 +586,38 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       tmem_ld_wait();
       const float inv =
           1.f / (__uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps);
-      const int t_glob = (c0 + i) * C + r;
-      const bool t_valid = t_glob < args.T;
-      __nv_bfloat16* orow = args.out + (((int64_t)b * args.T + t_glob) * args.H + h) * D;
+      // Stage the normalised rows in this chunk's Q tile (its last readers,
+      // MMA1/MMA2/MMA2b, completed before barO) ...
+      const int st = i & 1;
+      uint8_t* stg = sQ + st * kTile;
 #pragma unroll 1
       for (int cc = 0; cc < D; cc += 64) {
         uint32_t va[32], vb[32];
         tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
         tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
         tmem_ld_wait();
-        if (t_valid) {
-          store_scaled_32(va, inv, orow + cc);
-          store_scaled_32(vb, inv, orow + cc + 32);
-        }
+        stage_scaled_32(va, inv, stg, r, cc);
+        stage_scaled_32(vb, inv, stg, r, cc + 32);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kOFree]);
+      if (lane == 0) mbar_arrive(&bars[kOFree]);  // O may be overwritten now
+      // ... and store this warp's 32 rows with TMA (rows past T are clipped).
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int t0 = (c0 + i) * C + 32 * q4;
+        if (t0 < args.T) {
+          for (int a = 0; a < 2; ++a)
+            tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();
+        }
+        mbar_arrive(&bars[kEmptyQ0 + st]);  // the Q tile may be refilled
+      }
+      __syncwarp();
     }
+    if (lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
     if (!ok) {
       report_status(args.status, FAKLA_ERR_TIMEOUT);
       *abort_flag = 1;
@@ -801,12 +863,13 @@ __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const flo
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H) {
-  // (B, T, H, 128) bf16 viewed as 4-D {d, h, t, b}; box = 64 d x 1 h x 128 t x 1 b.
+static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
+                          int box_t = C) {
+  // (B, T, H, 128) bf16 viewed as 4-D {d, h, t, b}; box = 64 d x 1 h x box_t t x 1 b.
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2,
                                  (cuuint64_t)T * H * D * 2};
-  const cuuint32_t box[4] = {64, 1, (cuuint32_t)C, 1};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)box_t, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
                            dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -838,9 +901,9 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
                               cudaStream_t stream, int* status, bool* encoded) {
-  CUtensorMap mQ, mK, mV;
+  CUtensorMap mQ, mK, mV, mO;
   const bool ok = make_map_bthd(&mQ, q, B, T, H) && make_map_bthd(&mK, k, B, T, H) &&
-                  make_map_bthd(&mV, v, B, T, H);
+                  make_map_bthd(&mV, v, B, T, H) && make_map_bthd(&mO, out, B, T, H, 32);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   const int64_t nchunks = (T + C - 1) / C;
@@ -876,7 +939,6 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
 
   ScanArgs a;
   a.temp = (const __nv_bfloat16*)temp;
-  a.out = (__nv_bfloat16*)out;
   a.S = S;
   a.z = z;
   a.seg_init = seg_init;
@@ -890,7 +952,7 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  scan_sm100_kernel<<<(unsigned)(B * H * G), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, a);
+  scan_sm100_kernel<<<(unsigned)(B * H * G), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, a);
   return cudaGetLastError();
 }
 
