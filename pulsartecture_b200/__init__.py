@@ -8,11 +8,11 @@ Layout:
   backend/     torch-tensor front end (reference: ultra_rwka.backend.interface)
   kernels/     FeatureMap / LearnablePositiveMap (reference: ultra_rwka.kernels)
   components/  LinearProjection (reference: ultra_rwka.components.projections)
-  attention/   TMLinKernelAttn, TemperatureFunction, fa_kla, fa_kla_decode
+  attention/   TMLinKernelAttn, TemperatureFunction, fa_kla, fa_kla_host, fa_kla_decode
                (reference: ultra_rwka.attention)
 """
 __version__ = "0.1.0"
 
-from .attention import TemperatureFunction, TMLinKernelAttn, fa_kla, fa_kla_decode  # noqa: F401,E402
+from .attention import TemperatureFunction, TMLinKernelAttn, fa_kla, fa_kla_decode, fa_kla_host  # noqa: F401,E402
 from .backend import fa_kla_attention  # noqa: F401,E402
 from .kernels import FeatureMap, LearnablePositiveMap  # noqa: F401,E402

@@ -28,6 +28,7 @@ from ..backend.interface import (
     fa_kla_attention_with_state,
     fa_kla_decode_step,
     fa_kla_prefill,
+    fa_kla_prefill_host,
     new_state,
 )
 from ..components.projections import LinearProjection
@@ -206,6 +207,19 @@ def fa_kla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[St
     out, st = fa_kla_prefill(q.contiguous(), k.contiguous(), v.contiguous(), phi_weight, phi_bias,
                              temp, state, True)
     return out, st
+
+
+def fa_kla_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[State] = None, *,
+                phi_weight: torch.Tensor, phi_bias: Optional[torch.Tensor] = None,
+                temp: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                micro_batch: int = 1) -> Tuple[torch.Tensor, State]:
+    """``fa_kla`` for inputs that live in host memory: q, k, v (and temp) on the
+    CPU, phi_weight/phi_bias on the GPU that runs the call; returns the output
+    in host memory and the state on the GPU. Transfers in both directions
+    overlap the compute of neighbouring groups of ``micro_batch`` sequences.
+    The output is complete once the current CUDA stream has reached the call.
+    """
+    return fa_kla_prefill_host(q, k, v, phi_weight, phi_bias, temp, state, True, out, micro_batch)
 
 
 def fa_kla_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: State, *,

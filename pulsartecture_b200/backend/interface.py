@@ -275,3 +275,115 @@ def device_status(stream: Optional[torch.cuda.Stream] = None) -> None:
     (e.g. a bounded wait that expired)."""
     s = stream if stream is not None else torch.cuda.current_stream()
     _lib.check(_lib.lib().fakla_device_status(s.cuda_stream))
+
+
+def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
+                        bias: Optional[torch.Tensor] = None, temp: Optional[torch.Tensor] = None,
+                        state: Optional[State] = None, return_state: bool = True,
+                        out: Optional[torch.Tensor] = None, micro_batch: int = 1, slots: int = 3):
+    """phi fused with FA-KLA on HOST tensors, transfers overlapped with compute.
+
+    q, k: (B, T, in_dim) or (B, T, H_in, Dk) on the CPU (pin them for
+    asynchronous copies); v: (B, T, H, Dv) on the CPU; temp: (B, T, H) on the
+    CPU or None; weight, bias and the optional input state on the GPU that
+    runs the call. Sequences are independent, so the batch is cut into groups
+    of ``micro_batch`` sequences that flow through ``slots`` device buffers:
+    the host->device copy of one group, the fused prefill of the previous one
+    and the device->host copy of the one before run on three streams at once
+    (the two copy directions use separate copy engines).
+
+    Returns (out, state): ``out`` is a (B, T, H, Dv) host tensor (pinned unless
+    given), state (S, z) on the GPU. Like a ``non_blocking`` copy, the call
+    returns once the work is queued; ``out`` is complete when the caller's
+    current stream reaches this point (e.g. after ``torch.cuda.synchronize()``).
+    """
+    _require(weight.is_cuda, "weight must be a CUDA tensor: it selects the GPU that runs the call")
+    dev = weight.device
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (temp, "temp")):
+        _require(t is None or t.device.type == "cpu", f"{n} must be a host (CPU) tensor")
+    _require(q.dim() >= 3 and k.shape == q.shape, "q and k must have the same (B, T, ...) shape")
+    _require(v.dim() == 4, "v must be 4D (B, T, H, Dv)")
+    B, T = q.shape[0], q.shape[1]
+    in_dim = 1
+    for s in q.shape[2:]:
+        in_dim *= s
+    _require(tuple(v.shape[:2]) == (B, T), "B, T dimensions must match for q/k/v")
+    H, Dv = v.shape[2], v.shape[3]
+    _require(weight.dim() == 2 and weight.shape[1] == in_dim, f"weight must be (H*M, {in_dim})")
+    _require(weight.shape[0] % H == 0, "weight rows must be divisible by the number of heads")
+    M = weight.shape[0] // H
+    _require(bias is None or (bias.device == dev and tuple(bias.shape) == (H * M,)), "bias must be (H*M,) on weight's GPU")
+    _require(temp is None or tuple(temp.shape) == (B, T, H), "temp must be (B, T, H)")
+    dt = q.dtype
+    _require(all(t is None or t.dtype == dt for t in (k, v, weight, bias, temp)), "All inputs must have the same dtype")
+    _require(all(t is None or t.is_contiguous() for t in (q, k, v, weight, bias, temp)), "All inputs must be contiguous")
+    _require(micro_batch >= 1 and slots >= 2, "micro_batch >= 1 and slots >= 2")
+    code = _dtype_code(q)
+    _check_state(state, B, H, M, Dv, dev)
+    if out is None:
+        out = torch.empty(B, T, H, Dv, dtype=dt, pin_memory=True)
+    _require(out.device.type == "cpu" and tuple(out.shape) == (B, T, H, Dv) and out.dtype == dt and out.is_contiguous(),
+             "out must be a contiguous (B, T, H, Dv) host tensor of the input dtype")
+    S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
+    if B * T == 0:
+        return out, ((S, z) if return_state else None)
+    L = _lib.lib()
+    mb = min(micro_batch, B)
+    ngroups = (B + mb - 1) // mb
+    ns = min(slots, ngroups)
+    ws_bytes = L.fakla_prefill_workspace_bytes(mb, T, in_dim, H, M, Dv, code)
+    with torch.cuda.device(dev):
+        main = torch.cuda.current_stream(dev)
+        s_in = torch.cuda.Stream(dev)
+        s_out = torch.cuda.Stream(dev)
+        # per slot: inputs, output, workspace (allocated on the main stream)
+        bq = [torch.empty((mb,) + tuple(q.shape[1:]), device=dev, dtype=dt) for _ in range(ns)]
+        bk = [torch.empty((mb,) + tuple(q.shape[1:]), device=dev, dtype=dt) for _ in range(ns)]
+        bv = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
+        bt = [torch.empty((mb, T, H), device=dev, dtype=dt) for _ in range(ns)] if temp is not None else None
+        bo = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
+        bw = [torch.empty(ws_bytes, device=dev, dtype=torch.uint8) for _ in range(ns)]
+        ready = torch.cuda.Event()
+        ready.record(main)  # state buffers / inputs on the main stream precede the copies
+        s_in.wait_event(ready)
+        in_done = [torch.cuda.Event() for _ in range(ngroups)]
+        comp_done = [torch.cuda.Event() for _ in range(ngroups)]
+        out_done = [torch.cuda.Event() for _ in range(ngroups)]
+        for j in range(ngroups):
+            b0, b1 = j * mb, min(B, (j + 1) * mb)
+            n = b1 - b0
+            sl = j % ns
+            # host -> device (slot inputs free once the prefill that used them ended)
+            if j >= ns:
+                s_in.wait_event(comp_done[j - ns])
+            with torch.cuda.stream(s_in):
+                bq[sl][:n].copy_(q[b0:b1], non_blocking=True)
+                bk[sl][:n].copy_(k[b0:b1], non_blocking=True)
+                bv[sl][:n].copy_(v[b0:b1], non_blocking=True)
+                if temp is not None:
+                    bt[sl][:n].copy_(temp[b0:b1], non_blocking=True)
+            in_done[j].record(s_in)
+            # fused prefill on the main stream (slot output free once copied out)
+            main.wait_event(in_done[j])
+            if j >= ns:
+                main.wait_event(out_done[j - ns])
+            Sj = None if S is None else S[b0:b1]
+            zj = None if z is None else z[b0:b1]
+            _lib.check(L.fakla_prefill(
+                _ptr(bq[sl]), _ptr(bk[sl]), _ptr(bv[sl]), None if temp is None else _ptr(bt[sl]),
+                _ptr(weight), _ptr(bias), _ptr(bo[sl]), _ptr(Sj), _ptr(zj),
+                n, T, in_dim, H, M, Dv, code, flags, _ptr(bw[sl]), ws_bytes, main.cuda_stream))
+            comp_done[j].record(main)
+            # device -> host
+            s_out.wait_event(comp_done[j])
+            with torch.cuda.stream(s_out):
+                out[b0:b1].copy_(bo[sl][:n], non_blocking=True)
+            out_done[j].record(s_out)
+        # the caller's stream waits for the last copies; side-stream buffers stay
+        # reserved until then
+        main.wait_event(out_done[ngroups - 1])
+        for bufs in (bq, bk, bv, bo, bw) + ((bt,) if bt is not None else ()):
+            for t in bufs:
+                t.record_stream(s_in)
+                t.record_stream(s_out)
+    return out, ((S, z) if return_state else None)

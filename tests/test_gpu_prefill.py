@@ -158,3 +158,47 @@ def test_native_library_is_loaded(cuda):
     _lib.lib()
     maps = open("/proc/self/maps").read()
     assert "libfakla.so" in maps
+
+
+@pytest.mark.parametrize("micro_batch", [1, 2])
+def test_prefill_host_streaming_matches_device_and_oracle(cuda, micro_batch):
+    """fa_kla_host: host q/k/v/temp in, host out, copies overlapped with compute
+    over groups of sequences (the last group ragged); same results as the
+    device call and the oracle, initial state carried per sequence."""
+    from pulsartecture_b200.attention import fa_kla, fa_kla_host
+
+    B, T, H, D = 3, 300, 2, 128
+    q = (gen((B, T, H, D), 120) / np.sqrt(D)).bfloat16()
+    k = (gen((B, T, H, D), 121) / np.sqrt(D)).bfloat16()
+    v = (gen((B, T, H, D), 122) / np.sqrt(D)).bfloat16()
+    g = torch.Generator().manual_seed(123)
+    tp = (torch.rand(B, T, H, generator=g) + 0.5).bfloat16()
+    W, b = lpm_params(H * D, H * D, seed=124, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    S0 = (gen((B, H, D, D), 125) * 0.02 + 0.05).to(cuda)
+    z0 = (torch.rand(B, H, D, generator=g) * 20 + 10).to(cuda)
+    hq, hk, hv, ht = q.pin_memory(), k.pin_memory(), v.pin_memory(), tp.pin_memory()
+    out_h, (S_h, z_h) = fa_kla_host(hq, hk, hv, (S0, z0), phi_weight=W, phi_bias=b, temp=ht,
+                                    micro_batch=micro_batch)
+    torch.cuda.synchronize()
+    assert out_h.device.type == "cpu" and S_h.is_cuda
+    out_d, (S_d, z_d) = fa_kla(q.to(cuda), k.to(cuda), v.to(cuda), (S0, z0), phi_weight=W, phi_bias=b,
+                               temp=tp.to(cuda))
+    assert rel_l2(to_np(out_h), to_np(out_d)) < 2e-3
+    assert rel_l2(to_np(S_h), to_np(S_d)) < 1e-5
+    assert rel_l2(to_np(z_h), to_np(z_d)) < 1e-6
+    eo, eS, ez = O.prefill(to_np(q), to_np(k), to_np(v), to_np(W), to_np(b), to_np(tp), to_np(S0), to_np(z0))
+    assert rel_l2(to_np(out_h), eo) < BF16_REL_L2
+    assert np.abs(to_np(out_h) - eo).max() < BF16_MAX_ABS
+    assert rel_l2(to_np(S_h), eS) < BF16_REL_L2
+
+
+def test_prefill_host_rejects_device_inputs(cuda):
+    from pulsartecture_b200.attention import fa_kla_host
+
+    W, b = lpm_params(256, 256, seed=1, dtype=torch.bfloat16)
+    x = torch.zeros(1, 4, 256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="host"):
+        fa_kla_host(x.to(cuda), x, torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), phi_weight=W.to(cuda))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fa_kla_host(x, x, torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), phi_weight=W)
