@@ -45,6 +45,10 @@ DEC_N, DEC_H, DEC_STEPS = 256, 32, 1024
 DEC_IN = DEC_H * D
 METRIC = "FA-KLA prefill tokens/s"
 UNIT = "tokens/s"
+# DRAM bytes (read + write) per launch from one ncu capture of each kernel on
+# these shapes (dram__bytes_read.sum + dram__bytes_write.sum), committed in
+# profiles/phi_gemm_sm100_cfg2.md and profiles/scan_sm100_cfg2.md.
+PROFILED_DRAM_BYTES = {"phi_gemm_sm100": 276.9e6 + 233.4e6, "scan_sm100": 402.7e6 + 109.2e6}
 
 
 def peaks():
@@ -158,8 +162,9 @@ def cpu_reference_sample(t_len: int, threads: int | None = None):
     oracle/_ref. Returns (tokens, seconds, kind, cores)."""
     from oracle import build_ref
 
-    if threads:
-        torch.set_num_threads(threads)
+    # all host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
+    # per rank; the CPU baseline runs on rank 0 alone and should use them all)
+    torch.set_num_threads(threads or len(os.sched_getaffinity(0)))
     cores = torch.get_num_threads()
     W, b = lpm_init(IN_DIM, H * D)
     g = torch.Generator().manual_seed(1234)
@@ -286,6 +291,76 @@ def run_only(args):
     return 0
 
 
+def run_sustained(args):
+    """phi, scan and the phi+scan step of config 2, each launched back to back
+    for about 1.5 s while NVML samples SM clock, power and throttle reasons
+    every 5 ms (middle half of each run reported): how the kernels behave once
+    the part sits at its power cap, next to the burst numbers of the main line."""
+    import pynvml
+    from pulsartecture_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pynvml.nvmlInit()
+    hnd = pynvml.nvmlDeviceGetHandleByIndex(0)
+    L = _lib.lib()
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = (torch.randn(2 * B * T, IN_DIM, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    W, bias = lpm_init(IN_DIM, H * D)
+    W, bias = W.bfloat16().to(dev), bias.bfloat16().to(dev)
+    ph = torch.empty(2 * B * T, H * D, device=dev, dtype=torch.bfloat16)
+    v = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    out = torch.empty_like(v)
+    S = torch.empty(B, H, D, D, device=dev)
+    z = torch.empty(B, H, D, device=dev)
+
+    def phi():
+        _lib.check(L.fakla_phi(x.data_ptr(), W.data_ptr(), bias.data_ptr(), None, ph.data_ptr(),
+                               2 * B * T, IN_DIM, H * D, H, _lib.FAKLA_BF16, sh))
+
+    def scan():
+        _lib.check(L.fakla_attention(ph.data_ptr(), ph[B * T:].data_ptr(), v.data_ptr(), None, out.data_ptr(),
+                                     S.data_ptr(), z.data_ptr(), B, T, H, D, D, _lib.FAKLA_BF16,
+                                     _lib.FAKLA_STATE_OUT, None, 0, sh))
+
+    def step():
+        phi()
+        scan()
+
+    res = {}
+    for name, fn, n in (("phi_gemm_sm100", phi, 3200), ("scan_sm100", scan, 11000), ("step", step, 2500)):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        samples = []
+        stop = threading.Event()
+
+        def sample():
+            while not stop.is_set():
+                samples.append((pynvml.nvmlDeviceGetClockInfo(hnd, pynvml.NVML_CLOCK_SM),
+                                pynvml.nvmlDeviceGetPowerUsage(hnd) / 1000.0,
+                                int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(hnd))))
+                time.sleep(0.005)
+
+        th = threading.Thread(target=sample, daemon=True)
+        th.start()
+        ms = time_loop(fn, n, torch.cuda.current_stream(dev)) / n
+        stop.set()
+        th.join()
+        mid = samples[len(samples) // 4: 3 * len(samples) // 4] or samples
+        bits = 0
+        for _, _, r in mid:
+            bits |= r
+        res[name] = {"ms_per_launch": ms, "sm_mhz": statistics.median(c for c, _, _ in mid),
+                     "power_w": statistics.median(p for _, p, _ in mid),
+                     "reasons": [nm for bit, nm in ClockSampler.REASONS.items() if bits & bit and nm != "gpu_idle"],
+                     "samples": len(mid)}
+    _lib.check(L.fakla_device_status(sh))
+    print(json.dumps({"only": "sustained", **res}), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -297,11 +372,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode"],
-                    help="launch just one kernel (warmup + steps launches); for profiler captures")
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "sustained"],
+                    help="launch just one kernel (warmup + steps launches) for profiler captures; "
+                         "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.only == "sustained":
+        return run_sustained(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
@@ -483,13 +561,16 @@ def main():
             "config": workload_config(world),
             "roofline": {"bound": "tensor", "kernel": "phi_gemm_sm100 (phi(q), phi(k): 2*65536 x 2048 x 2048)",
                          "achieved": phi_tflops, "peak": tflops_burst, "unit": "TFLOP/s",
-                         "frac": phi_tflops / tflops_burst, "traffic": None,
+                         "frac": phi_tflops / tflops_burst, "traffic": PROFILED_DRAM_BYTES["phi_gemm_sm100"],
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                           "(profiles/phi_gemm_sm100_cfg2.md)",
                          "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS"},
             "kernels": {
                 "phi_gemm_sm100": {"ms": phi_ms, "flops": phi_flops, "tflops": phi_tflops,
                                    "frac_of_peak": phi_tflops / tflops_burst},
                 "scan_sm100": {"ms": scan_ms, "bytes": scan_bytes, "gbs": scan_gbs, "frac_of_hbm": scan_gbs / hbm_gbs,
-                               "tflops": attn_flops / (scan_ms * 1e-3) / 1e12},
+                               "tflops": attn_flops / (scan_ms * 1e-3) / 1e12,
+                               "traffic": PROFILED_DRAM_BYTES["scan_sm100"]},
                 "sum_ms": phi_ms + scan_ms,
             },
             "e2e": e2e,
