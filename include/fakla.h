@@ -125,6 +125,57 @@ int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
               void* out, int64_t rows, int64_t in_dim, int64_t feat_dim,
               int64_t heads, int dtype, void* stream);
 
+/* Output activation of fakla_feature_map. */
+typedef enum {
+  FAKLA_ACT_ELU1 = 0,     /* elu(x) + 1                        (feature_maps.py:248) */
+  FAKLA_ACT_RELU = 1,     /* max(x, 0)                         (feature_maps.py:250) */
+  FAKLA_ACT_SOFTPLUS = 2, /* log(1 + e^x), x for x > 20        (feature_maps.py:252) */
+  FAKLA_ACT_GELU = 3,     /* x/2 (1 + erf(x/sqrt 2))           (feature_maps.py:254, 239) */
+  FAKLA_ACT_IDENTITY = 4, /* x                                 (gate logits, mixer.py:60-66) */
+  FAKLA_ACT_SIGMOID = 5,  /* 1 / (1 + e^-x)                    (tm_kla.py:89) */
+  FAKLA_ACT_ABS = 6,      /* |x|                               (tm_kla.py:89) */
+  FAKLA_ACT_COSSIN = 7    /* [cos x, sin x] * scale            (feature_maps.py:30-37) */
+} fakla_activation;
+
+/*
+ * fakla_feature_map -- one linear layer with its output activation,
+ * out = act(x W^T + bias).
+ *
+ * Replaces: one layer of LearnablePositiveMap's MLP and its final activation
+ *   (ultra_rwka/kernels/feature_maps.py:234-268, all four activations; hidden
+ *   layers use FAKLA_ACT_GELU, feature_maps.py:239); the projection of
+ *   RandomFourierFeatures / OrthogonalRandomFeatures (_rff_forward_script,
+ *   feature_maps.py:30-37, with W given transposed); the layers of GateNet
+ *   (kernels/mixer.py:11-66) and of TemperatureFunction (attention/
+ *   tm_kla.py:17-107).
+ *
+ *   x    : (rows, in_dim)    W : (n_out, in_dim) (nn.Linear weight layout)
+ *   bias : (n_out) or NULL
+ *   out  : (rows, n_out), or (rows, 2 * n_out) for FAKLA_ACT_COSSIN: column n
+ *          holds scale * cos(p_n) and column n_out + n holds scale * sin(p_n),
+ *          p = x W^T + bias. `scale` is ignored by the other activations.
+ * The tensor-core path serves BF16 with in_dim % 64 == 0, n_out % 256 == 0
+ * and 16-byte aligned pointers; other shapes and F32 run on CUDA cores.
+ */
+int fakla_feature_map(const void* x, const void* W, const void* bias, void* out,
+                      int64_t rows, int64_t in_dim, int64_t n_out, int act,
+                      float scale, int dtype, void* stream);
+
+/*
+ * fakla_mix_features -- the KernelFeatureMixer combination
+ * out = sum_i softmax(logits)_i * feats_i.
+ *
+ * Replaces: the softmax gate and the weighted sum of KernelFeatureMixer
+ *   (ultra_rwka/kernels/mixer.py:118-150 / 236-248): the softmax runs in fp32
+ *   and its weights are rounded to `dtype` before the sum, as the reference's
+ *   softmax(logits.float()).to(logits.dtype) does.
+ *
+ *   feats  : (n_maps, rows, feat_dim), map i's features in slice i
+ *   logits : (rows, n_maps) gate logits     out : (rows, feat_dim)
+ */
+int fakla_mix_features(const void* feats, const void* logits, void* out, int64_t rows,
+                       int64_t n_maps, int64_t feat_dim, int dtype, void* stream);
+
 /*
  * fakla_prefill -- feature map fused with FA-KLA: the hot path of
  * TMLinKernelAttn.forward from the projected q/k/v onward (ultra_rwka/

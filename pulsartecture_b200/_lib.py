@@ -18,6 +18,16 @@ FAKLA_BF16 = 1
 FAKLA_STATE_IN = 1
 FAKLA_STATE_OUT = 2
 
+# fakla_activation (include/fakla.h)
+FAKLA_ACT_ELU1 = 0
+FAKLA_ACT_RELU = 1
+FAKLA_ACT_SOFTPLUS = 2
+FAKLA_ACT_GELU = 3
+FAKLA_ACT_IDENTITY = 4
+FAKLA_ACT_SIGMOID = 5
+FAKLA_ACT_ABS = 6
+FAKLA_ACT_COSSIN = 7
+
 STATUS = {
     0: "FAKLA_OK",
     1: "FAKLA_ERR_INVALID_ARG",
@@ -43,6 +53,8 @@ SIGNATURES = {
     "fakla_attention": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),
     "fakla_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "fakla_phi": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
+    "fakla_feature_map": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, ctypes.c_float, _int, _p]),
+    "fakla_mix_features": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "fakla_prefill": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),
     "fakla_prefill_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
     "fakla_decode_mapped": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),

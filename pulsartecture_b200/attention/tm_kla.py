@@ -32,7 +32,7 @@ from ..backend.interface import (
     new_state,
 )
 from ..components.projections import LinearProjection
-from ..kernels.feature_maps import FeatureMap, LearnablePositiveMap
+from ..kernels.feature_maps import FeatureMap, LearnablePositiveMap, run_mlp
 
 
 class TemperatureFunction(nn.Module):
@@ -77,7 +77,9 @@ class TemperatureFunction(nn.Module):
         expected = next(self.parameters()).dtype
         if x.dtype != expected:
             x = x.to(dtype=expected)
-        return self.final_activation_fn(self.network(x))
+        # every Linear with the activation after it (the last one with the
+        # final activation) is one fakla_feature_map launch
+        return run_mlp(x, self.network, self.final_activation_type)
 
 
 class TMLinKernelAttn(nn.Module):

@@ -387,3 +387,72 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
                 t.record_stream(s_in)
                 t.record_stream(s_out)
     return out, ((S, z) if return_state else None)
+
+
+# ----------------------------------------------------------------------------- feature-map family
+ACTIVATIONS = {
+    "elu+1": _lib.FAKLA_ACT_ELU1, "relu": _lib.FAKLA_ACT_RELU, "softplus": _lib.FAKLA_ACT_SOFTPLUS,
+    "gelu": _lib.FAKLA_ACT_GELU, "identity": _lib.FAKLA_ACT_IDENTITY, "sigmoid": _lib.FAKLA_ACT_SIGMOID,
+    "abs": _lib.FAKLA_ACT_ABS, "cossin": _lib.FAKLA_ACT_COSSIN,
+}
+
+
+def feature_map(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                act: str = "elu+1", scale: float = 1.0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """act(x W^T + b) in one launch of fakla_feature_map.
+
+    x: (..., in_dim); weight: (n_out, in_dim) (nn.Linear layout); bias: (n_out,)
+    or None. Returns (..., n_out), or (..., 2*n_out) for act="cossin" (scale *
+    [cos p, sin p], the random-Fourier-feature form of feature_maps.py:30-37).
+    ``out`` (contiguous, right shape) is written in place when given.
+    """
+    _require(act in ACTIVATIONS, f"unknown activation {act!r}; choose from {sorted(ACTIVATIONS)}")
+    _require(weight.dim() == 2, "weight must be (n_out, in_dim)")
+    n_out, in_dim = weight.shape
+    _require(x.shape[-1] == in_dim, f"x last dim {x.shape[-1]} != in_dim {in_dim}")
+    _require(bias is None or tuple(bias.shape) == (n_out,), "bias must be (n_out,)")
+    dev = _check_device([x, weight, bias, out], ["x", "weight", "bias", "out"])
+    dt = x.dtype
+    _require(all(t is None or t.dtype == dt for t in (weight, bias, out)), "All inputs must have the same dtype")
+    code = _dtype_code(x)
+    x = x.contiguous()
+    weight = weight.contiguous()
+    bias = None if bias is None else bias.contiguous()
+    lead = x.shape[:-1]
+    rows = 1
+    for s in lead:
+        rows *= s
+    cols = 2 * n_out if act == "cossin" else n_out
+    if out is None:
+        out = torch.empty(*lead, cols, device=dev, dtype=dt)
+    _require(out.is_contiguous() and out.numel() == rows * cols, "out must be a contiguous (..., n_out) tensor")
+    if rows == 0:
+        return out
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_feature_map(_ptr(x), _ptr(weight), _ptr(bias), _ptr(out), rows, in_dim, n_out,
+                                       ACTIVATIONS[act], float(scale), code, _stream(dev)))
+    return out
+
+
+def mix_features(feats: torch.Tensor, logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """sum_i softmax(logits)_i * feats[i] (KernelFeatureMixer, mixer.py:118-150).
+
+    feats: (n_maps, rows, F); logits: (rows, n_maps), same dtype. Returns (rows, F).
+    """
+    _require(feats.dim() == 3, "feats must be (n_maps, rows, F)")
+    n_maps, rows, F = feats.shape
+    _require(tuple(logits.shape) == (rows, n_maps), f"logits must be (rows, n_maps) = {(rows, n_maps)}")
+    dev = _check_device([feats, logits, out], ["feats", "logits", "out"])
+    _require(logits.dtype == feats.dtype, "feats and logits must have the same dtype")
+    code = _dtype_code(feats)
+    feats = feats.contiguous()
+    logits = logits.contiguous()
+    if out is None:
+        out = torch.empty(rows, F, device=dev, dtype=feats.dtype)
+    if rows == 0:
+        return out
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        _lib.check(L.fakla_mix_features(_ptr(feats), _ptr(logits), _ptr(out), rows, n_maps, F, code, _stream(dev)))
+    return out

@@ -230,21 +230,24 @@ int run_attention(const void* q, const void* k, const void* v, const void* temp,
   return FAKLA_OK;
 }
 
-// phi for one or two row sets sharing W (q rows -> out0, k rows -> out1 with temp1).
+// phi for one or two row sets sharing W (q rows -> out0, k rows -> out1 with
+// temp1); act is a FAKLA_ACT_* code (FAKLA_ACT_ELU1 for FA-KLA).
 int run_phi(const void* x0, const void* x1, const void* W, const void* bias, const void* temp0,
             const void* temp1, void* out0, void* out1, int64_t rows, int64_t K, int64_t N,
-            int64_t heads, int dtype, cudaStream_t stream, DeviceInfo* d) {
+            int64_t heads, int dtype, cudaStream_t stream, DeviceInfo* d,
+            int act = FAKLA_ACT_ELU1, float scale = 1.f) {
   if (use_sm100_phi(dtype, x0, x1, W, out0, out1, bias, rows, K, N, heads)) {
     bool enc = false;
     cudaError_t e = fakla::launch_phi_sm100(x0, x1, W, bias, temp0, temp1, out0, out1, rows, K,
-                                            N, heads, stream, d->status, &enc);
+                                            N, heads, act, scale, stream, d->status, &enc);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "phi_sm100 launch");
     return FAKLA_OK;
   }
-  cudaError_t e = fakla::launch_phi_simt(dtype, x0, W, bias, temp0, out0, rows, K, N, heads, stream);
+  cudaError_t e =
+      fakla::launch_phi_simt(dtype, x0, W, bias, temp0, out0, rows, K, N, heads, act, scale, stream);
   if (e == cudaSuccess && x1 != nullptr)
-    e = fakla::launch_phi_simt(dtype, x1, W, bias, temp1, out1, rows, K, N, heads, stream);
+    e = fakla::launch_phi_simt(dtype, x1, W, bias, temp1, out1, rows, K, N, heads, act, scale, stream);
   if (e != cudaSuccess) return cuda_fail(e, "phi_simt launch");
   return FAKLA_OK;
 }
@@ -302,6 +305,44 @@ extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const v
   if ((rc = require_device(&d))) return rc;
   return run_phi(x, nullptr, W, bias, temp, nullptr, out, nullptr, rows, in_dim, feat_dim, heads,
                  dtype, (cudaStream_t)stream, d);
+}
+
+extern "C" int fakla_feature_map(const void* x, const void* W, const void* bias, void* out,
+                                 int64_t rows, int64_t in_dim, int64_t n_out, int act, float scale,
+                                 int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!x || !W || !out)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "x, W and out must be non-NULL");
+  if (act < FAKLA_ACT_ELU1 || act > FAKLA_ACT_COSSIN)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "unknown activation %d", act);
+  if (rows < 1 || in_dim < 1 || n_out < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "bad sizes rows=%lld in_dim=%lld n_out=%lld",
+                           (long long)rows, (long long)in_dim, (long long)n_out);
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  return run_phi(x, nullptr, W, bias, nullptr, nullptr, out, nullptr, rows, in_dim, n_out, 1,
+                 dtype, (cudaStream_t)stream, d, act, scale);
+}
+
+extern "C" int fakla_mix_features(const void* feats, const void* logits, void* out, int64_t rows,
+                                  int64_t n_maps, int64_t feat_dim, int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!feats || !logits || !out)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "feats, logits and out must be non-NULL");
+  if (rows < 1 || feat_dim < 1 || n_maps < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "bad sizes rows=%lld n_maps=%lld feat_dim=%lld",
+                           (long long)rows, (long long)n_maps, (long long)feat_dim);
+  if (!fakla::mix_supported(n_maps))
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "at most 32 feature maps can be mixed, got %lld",
+                           (long long)n_maps);
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_mix_features(dtype, feats, logits, out, rows, n_maps, feat_dim,
+                                             (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "mix_features launch");
+  return FAKLA_OK;
 }
 
 extern "C" size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim, int64_t H,

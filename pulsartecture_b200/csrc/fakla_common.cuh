@@ -33,6 +33,29 @@ __device__ __forceinline__ float elu_plus_one_fast(float x) {
   return x > 0.f ? x + 1.f : __expf(x);
 }
 
+// Output activations of the feature-map GEMMs (FAKLA_ACT_* in fakla.h),
+// written from their definitions: torch's elu(alpha=1)+1, relu,
+// softplus(beta=1, threshold=20), exact (erf) gelu, sigmoid and abs. kFast
+// uses the hardware exp approximation where the result is rounded to bf16.
+template <int ACT, bool kFast>
+__device__ __forceinline__ float activate(float x) {
+  if constexpr (ACT == FAKLA_ACT_ELU1) {
+    return kFast ? elu_plus_one_fast(x) : elu_plus_one(x);
+  } else if constexpr (ACT == FAKLA_ACT_RELU) {
+    return x > 0.f ? x : 0.f;
+  } else if constexpr (ACT == FAKLA_ACT_SOFTPLUS) {
+    return x > 20.f ? x : log1pf(expf(x));
+  } else if constexpr (ACT == FAKLA_ACT_GELU) {
+    return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+  } else if constexpr (ACT == FAKLA_ACT_SIGMOID) {
+    return 1.f / (1.f + expf(-x));
+  } else if constexpr (ACT == FAKLA_ACT_ABS) {
+    return fabsf(x);
+  } else {
+    return x;  // FAKLA_ACT_IDENTITY (COSSIN is handled by the callers)
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);
 template <>

@@ -14,9 +14,14 @@ bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t ran
                        CUtensorMapSwizzle swizzle);
 
 // CUDA-core kernels (simt_kernels.cu)
+// act: FAKLA_ACT_*; for FAKLA_ACT_COSSIN, out has 2N columns (cos, then sin)
+// scaled by `scale`.
 cudaError_t launch_phi_simt(int dtype, const void* x, const void* W, const void* bias,
                             const void* temp, void* out, int64_t rows, int64_t K, int64_t N,
-                            int64_t heads, cudaStream_t stream);
+                            int64_t heads, int act, float scale, cudaStream_t stream);
+bool mix_supported(int64_t n_maps);
+cudaError_t launch_mix_features(int dtype, const void* feats, const void* logits, void* out,
+                                int64_t rows, int64_t n_maps, int64_t F, cudaStream_t stream);
 bool scan_simt_supported(int64_t Df, int64_t Dv);
 size_t scan_simt_smem_bytes(int64_t Df, int64_t Dv);
 cudaError_t launch_scan_simt(int dtype, const void* q, const void* k, const void* v,
@@ -31,8 +36,8 @@ cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v
 bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads);
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
                              const void* temp0, const void* temp1, void* out0, void* out1,
-                             int64_t rows, int64_t K, int64_t N, int64_t heads,
-                             cudaStream_t stream, int* status, bool* encoded);
+                             int64_t rows, int64_t K, int64_t N, int64_t heads, int act,
+                             float scale, cudaStream_t stream, int* status, bool* encoded);
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
 // Segments per sequence the scan uses on a device with `sms` SMs (1 = one CTA
 // per sequence), and the workspace that takes (0 when G = 1).

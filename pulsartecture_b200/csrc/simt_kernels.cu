@@ -23,11 +23,11 @@ namespace {
 constexpr int kPhiTile = 64;
 constexpr int kPhiK = 16;
 
-template <typename T>
+template <typename T, int ACT>
 __global__ void __launch_bounds__(256) phi_simt_kernel(
     const T* __restrict__ x, const T* __restrict__ W, const T* __restrict__ bias,
     const T* __restrict__ temp, T* __restrict__ out, int64_t rows, int64_t K,
-    int64_t N, int64_t heads) {
+    int64_t N, int64_t heads, float scale) {
   __shared__ float xs[kPhiK][kPhiTile + 4];
   __shared__ float ws[kPhiK][kPhiTile + 4];
   const int tid = threadIdx.x;
@@ -71,10 +71,16 @@ __global__ void __launch_bounds__(256) phi_simt_kernel(
     for (int j = 0; j < 4; ++j) {
       const int64_t gc = col0 + tc * 4 + j;
       if (gc >= N) continue;
-      float val = acc[i][j] + (bias ? to_f32(bias[gc]) : 0.f);
-      val = elu_plus_one(val);
-      if (temp) val *= to_f32(temp[gr * heads + gc / m]);
-      out[gr * N + gc] = from_f32<T>(val);
+      const float pre = acc[i][j] + (bias ? to_f32(bias[gc]) : 0.f);
+      const float tv = temp ? to_f32(temp[gr * heads + gc / m]) : 1.f;
+      if constexpr (ACT == FAKLA_ACT_COSSIN) {
+        float sn, cs;
+        sincosf(pre, &sn, &cs);
+        out[gr * 2 * N + gc] = from_f32<T>(cs * scale * tv);
+        out[gr * 2 * N + N + gc] = from_f32<T>(sn * scale * tv);
+      } else {
+        out[gr * N + gc] = from_f32<T>(activate<ACT, false>(pre) * tv);
+      }
     }
   }
 }
@@ -304,23 +310,111 @@ __global__ void __launch_bounds__(256) decode_kernel(
 // ---------------------------------------------------------------------------
 // Launchers (host). Shapes were validated by the caller (fakla_api.cu).
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int ACT>
 static cudaError_t launch_phi_simt_t(const void* x, const void* W, const void* bias,
                                      const void* temp, void* out, int64_t rows,
-                                     int64_t K, int64_t N, int64_t heads,
+                                     int64_t K, int64_t N, int64_t heads, float scale,
                                      cudaStream_t stream) {
   dim3 grid((unsigned)((N + kPhiTile - 1) / kPhiTile), (unsigned)((rows + kPhiTile - 1) / kPhiTile));
-  phi_simt_kernel<T><<<grid, 256, 0, stream>>>(
-      (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads);
+  phi_simt_kernel<T, ACT><<<grid, 256, 0, stream>>>(
+      (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads, scale);
   return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_phi_simt_dt(int act, const void* x, const void* W, const void* bias,
+                                      const void* temp, void* out, int64_t rows, int64_t K,
+                                      int64_t N, int64_t heads, float scale, cudaStream_t stream) {
+#define FAKLA_PHI_CASE(A) \
+  case A: return launch_phi_simt_t<T, A>(x, W, bias, temp, out, rows, K, N, heads, scale, stream);
+  switch (act) {
+    FAKLA_PHI_CASE(FAKLA_ACT_ELU1)
+    FAKLA_PHI_CASE(FAKLA_ACT_RELU)
+    FAKLA_PHI_CASE(FAKLA_ACT_SOFTPLUS)
+    FAKLA_PHI_CASE(FAKLA_ACT_GELU)
+    FAKLA_PHI_CASE(FAKLA_ACT_IDENTITY)
+    FAKLA_PHI_CASE(FAKLA_ACT_SIGMOID)
+    FAKLA_PHI_CASE(FAKLA_ACT_ABS)
+    FAKLA_PHI_CASE(FAKLA_ACT_COSSIN)
+    default: return cudaErrorInvalidValue;
+  }
+#undef FAKLA_PHI_CASE
 }
 
 cudaError_t launch_phi_simt(int dtype, const void* x, const void* W, const void* bias,
                             const void* temp, void* out, int64_t rows, int64_t K,
-                            int64_t N, int64_t heads, cudaStream_t stream) {
+                            int64_t N, int64_t heads, int act, float scale, cudaStream_t stream) {
   if (dtype == FAKLA_BF16)
-    return launch_phi_simt_t<__nv_bfloat16>(x, W, bias, temp, out, rows, K, N, heads, stream);
-  return launch_phi_simt_t<float>(x, W, bias, temp, out, rows, K, N, heads, stream);
+    return launch_phi_simt_dt<__nv_bfloat16>(act, x, W, bias, temp, out, rows, K, N, heads, scale, stream);
+  return launch_phi_simt_dt<float>(act, x, W, bias, temp, out, rows, K, N, heads, scale, stream);
+}
+
+// ---------------------------------------------------------------------------
+// KernelFeatureMixer combination: out[r, f] = sum_i w_i(r) feats[i, r, f] with
+// w(r) = softmax(logits[r, :]) in fp32, rounded to T (as the reference's
+// softmax(logits.float()).to(logits.dtype), mixer.py:134-135), and the sum
+// accumulated in fp32. One thread per (row, VEC consecutive features); the
+// weights of a row are recomputed per thread (n_maps is a handful).
+// ---------------------------------------------------------------------------
+constexpr int kMaxMaps = 32;
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) mix_features_kernel(const T* __restrict__ feats,
+                                                           const T* __restrict__ logits,
+                                                           T* __restrict__ out, int64_t rows,
+                                                           int n_maps, int64_t F) {
+  const int64_t per_row = F / VEC;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const int64_t r = idx / per_row;
+  const int64_t f0 = (idx % per_row) * VEC;
+  float w[kMaxMaps];
+  float mx = -INFINITY;
+  for (int i = 0; i < n_maps; ++i) {
+    w[i] = to_f32(logits[r * n_maps + i]);
+    mx = fmaxf(mx, w[i]);
+  }
+  float den = 0.f;
+  for (int i = 0; i < n_maps; ++i) {
+    w[i] = expf(w[i] - mx);
+    den += w[i];
+  }
+  const float inv = 1.f / den;
+  float acc[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+  for (int i = 0; i < n_maps; ++i) {
+    const float wi = to_f32(from_f32<T>(w[i] * inv));
+    const T* src = feats + ((int64_t)i * rows + r) * F + f0;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[v] = fmaf(wi, to_f32(src[v]), acc[v]);
+  }
+  T* dst = out + r * F + f0;
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) dst[v] = from_f32<T>(acc[v]);
+}
+
+template <typename T>
+static cudaError_t launch_mix_t(const void* feats, const void* logits, void* out, int64_t rows,
+                                int64_t n_maps, int64_t F, cudaStream_t stream) {
+  const bool vec = F % 8 == 0 && ((uintptr_t)feats & 15u) == 0 && ((uintptr_t)out & 15u) == 0;
+  const int64_t threads = rows * (vec ? F / 8 : F);
+  const unsigned grid = (unsigned)((threads + 255) / 256);
+  if (vec)
+    mix_features_kernel<T, 8><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
+                                                       rows, (int)n_maps, F);
+  else
+    mix_features_kernel<T, 1><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
+                                                       rows, (int)n_maps, F);
+  return cudaGetLastError();
+}
+
+bool mix_supported(int64_t n_maps) { return n_maps >= 1 && n_maps <= kMaxMaps; }
+
+cudaError_t launch_mix_features(int dtype, const void* feats, const void* logits, void* out,
+                                int64_t rows, int64_t n_maps, int64_t F, cudaStream_t stream) {
+  if (dtype == FAKLA_BF16) return launch_mix_t<__nv_bfloat16>(feats, logits, out, rows, n_maps, F, stream);
+  return launch_mix_t<float>(feats, logits, out, rows, n_maps, F, stream);
 }
 
 bool scan_simt_supported(int64_t Df, int64_t Dv) {

@@ -1,12 +1,16 @@
-// phi GEMM on the sm_100a tensor cores: out = elu(x W^T + bias) + 1 [* temp].
+// phi GEMM on the sm_100a tensor cores: out = act(x W^T + bias) [* temp].
 //
 // The feature map of the default FA-KLA configuration is one nn.Linear over
 // the full H*Dk projected row followed by elu+1 (LearnablePositiveMap,
 // ultra_rwka/kernels/feature_maps.py:224,248,259-268); at B=8, T=4096,
 // H*Dk=2048 it is ~90% of the FA-KLA FLOPs. This kernel computes it for up to
 // two row sets in one launch (q rows and k rows share W), with the bias,
-// the elu+1 activation and the k-side temperature (k~ = phi(k) * temp,
-// cpu_kernels.cpp:121-123) fused into the epilogue, and writes bf16.
+// the activation and the k-side temperature (k~ = phi(k) * temp,
+// cpu_kernels.cpp:121-123) fused into the epilogue, and writes bf16. The
+// activation is a template parameter: elu+1 for FA-KLA, and the other
+// FAKLA_ACT_* forms for the rest of the feature-map family (LearnablePositive
+// Map's relu/softplus/gelu, MLP hidden layers, gate logits, and the cos/sin
+// pairs of random Fourier features, written to columns n and N + n).
 //
 // Structure: persistent CTAs (one per SM), 10 warps:
 //   warp 0      TMA producer: 128x64 x-tile + 256x64 W-tile per stage (4 stages)
@@ -51,12 +55,14 @@ constexpr size_t kSmemBytes = 1024 /*align slack*/ + (size_t)kStages * kStageByt
 
 struct PhiArgs {
   const __nv_bfloat16* bias;   // [N] or null
+  float scale;                 // FAKLA_ACT_COSSIN output scale
   const __nv_bfloat16* temp0;  // [rows, heads] or null (row set 0)
   const __nv_bfloat16* temp1;  // [rows, heads] or null (row set 1)
   int rows, N, K, heads, nsets;
   int* status;
 };
 
+template <int ACT>
 __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC0,
@@ -244,31 +250,43 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
 #pragma unroll
           for (int i = 0; i < 32; ++i) bw[i] = 0u;
         }
-        uint32_t packed[32];
+        // Two passes for FAKLA_ACT_COSSIN (cos to column c0, sin to column
+        // N + c0), one for every other activation.
+        constexpr int kPasses = ACT == FAKLA_ACT_COSSIN ? 2 : 1;
+#pragma unroll 1
+        for (int pass = 0; pass < kPasses; ++pass) {
+          uint32_t packed[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint32_t raw_a = i < 16 ? v0[2 * i] : v1[2 * i - 32];
-          const uint32_t raw_b = i < 16 ? v0[2 * i + 1] : v1[2 * i + 1 - 32];
-          const float a = __uint_as_float(raw_a) + __uint_as_float(bw[i] << 16);
-          const float b = __uint_as_float(raw_b) + __uint_as_float(bw[i] & 0xffff0000u);
-          packed[i] = pack_bf16x2(elu_plus_one_fast(a) * tscale, elu_plus_one_fast(b) * tscale);
-        }
-        // single staging buffer per warp: the previous store must have read it
-        if (lane == 0 && stored) bulk_wait_group_read<0>();
-        __syncwarp();
+          for (int i = 0; i < 32; ++i) {
+            const uint32_t raw_a = i < 16 ? v0[2 * i] : v1[2 * i - 32];
+            const uint32_t raw_b = i < 16 ? v0[2 * i + 1] : v1[2 * i + 1 - 32];
+            const float a = __uint_as_float(raw_a) + __uint_as_float(bw[i] << 16);
+            const float b = __uint_as_float(raw_b) + __uint_as_float(bw[i] & 0xffff0000u);
+            if constexpr (ACT == FAKLA_ACT_COSSIN) {
+              const float fa = pass == 0 ? cosf(a) : sinf(a);
+              const float fb = pass == 0 ? cosf(b) : sinf(b);
+              packed[i] = pack_bf16x2(fa * args.scale * tscale, fb * args.scale * tscale);
+            } else {
+              packed[i] = pack_bf16x2(activate<ACT, true>(a) * tscale, activate<ACT, true>(b) * tscale);
+            }
+          }
+          // single staging buffer per warp: the previous store must have read it
+          if (lane == 0 && stored) bulk_wait_group_read<0>();
+          __syncwarp();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 val = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                                 packed[4 * c + 3]);
-          *reinterpret_cast<uint4*>(buf + sw128_offset((uint32_t)lane, (uint32_t)(c * 8))) = val;
+          for (int c = 0; c < 8; ++c) {
+            uint4 val = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                   packed[4 * c + 3]);
+            *reinterpret_cast<uint4*>(buf + sw128_offset((uint32_t)lane, (uint32_t)(c * 8))) = val;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(mapC, buf, c0 + pass * args.N, row0 + 32 * q);
+            bulk_commit_group();
+          }
+          stored = true;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(mapC, buf, c0, row0 + 32 * q);
-          bulk_commit_group();
-        }
-        stored = true;
       }
       if (++acc == 2) {
         acc = 0;
@@ -310,18 +328,31 @@ bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads) {
   return true;
 }
 
+template <int ACT>
+static cudaError_t launch_act(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
+                              const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
+                              int grid, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel<ACT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  phi_gemm_sm100_kernel<ACT><<<grid, kThreads, kSmemBytes, stream>>>(mA0, mA1, mB, mC0, mC1, a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
                              const void* temp0, const void* temp1, void* out0, void* out1,
-                             int64_t rows, int64_t K, int64_t N, int64_t heads,
-                             cudaStream_t stream, int* status, bool* encoded) {
+                             int64_t rows, int64_t K, int64_t N, int64_t heads, int act,
+                             float scale, cudaStream_t stream, int* status, bool* encoded) {
   CUtensorMap mA0, mA1, mB, mC0, mC1;
   const int nsets = x1 != nullptr ? 2 : 1;
+  const uint64_t out_cols = (uint64_t)N * (act == FAKLA_ACT_COSSIN ? 2 : 1);
   bool ok = make_map_2d(&mA0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) &&
             make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, BN) &&
-            make_map_2d(&mC0, out0, (uint64_t)N, (uint64_t)rows, 64, 32);
+            make_map_2d(&mC0, out0, out_cols, (uint64_t)rows, 64, 32);
   if (ok && nsets == 2)
     ok = make_map_2d(&mA1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-         make_map_2d(&mC1, out1, (uint64_t)N, (uint64_t)rows, 64, 32);
+         make_map_2d(&mC1, out1, out_cols, (uint64_t)rows, 64, 32);
   else {
     mA1 = mA0;
     mC1 = mC0;
@@ -330,6 +361,7 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   if (!ok) return cudaErrorInvalidValue;
   PhiArgs a;
   a.bias = (const __nv_bfloat16*)bias;
+  a.scale = scale;
   a.temp0 = (const __nv_bfloat16*)temp0;
   a.temp1 = (const __nv_bfloat16*)temp1;
   a.rows = (int)rows;
@@ -341,12 +373,17 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   const int row_tiles = (int)((rows + BM - 1) / BM);
   const int total = row_tiles * (int)(N / BN) * nsets;
   const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
-  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
-  phi_gemm_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mA0, mA1, mB, mC0, mC1, a);
-  return cudaGetLastError();
+  switch (act) {
+    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace fakla

@@ -1,2 +1,8 @@
-"""Feature maps (phi) for FA-KLA."""
-from .feature_maps import FeatureMap, LearnablePositiveMap  # noqa: F401
+"""Feature maps (phi) for FA-KLA and their dynamic mixture."""
+from .feature_maps import (  # noqa: F401
+    FeatureMap,
+    LearnablePositiveMap,
+    OrthogonalRandomFeatures,
+    RandomFourierFeatures,
+)
+from .mixer import GateNet, KernelFeatureMixer  # noqa: F401

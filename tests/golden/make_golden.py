@@ -56,6 +56,12 @@ def _load_file(name: str, path: str, package: str):
 
 def load_reference(ref_root: str, ref_kernel):
     """Import the reference's LearnablePositiveMap and TMLinKernelAttn."""
+    fm, _, tm = load_reference_modules(ref_root, ref_kernel)
+    return fm.LearnablePositiveMap, tm.TMLinKernelAttn
+
+
+def load_reference_modules(ref_root: str, ref_kernel):
+    """Import the reference's feature_maps, mixer and tm_kla modules."""
     pkg = os.path.join(ref_root, "ultra_rwka")
     for name, path in [
         ("ultra_rwka", pkg),
@@ -80,8 +86,8 @@ def load_reference(ref_root: str, ref_kernel):
     had_warnings = hasattr(builtins_mod, "warnings")
     builtins_mod.warnings = warnings  # mixer.py:183 uses `warnings` without importing it
     try:
-        _load_file("ultra_rwka.components.kernels.mixer", os.path.join(pkg, "kernels", "mixer.py"),
-                   "ultra_rwka.components.kernels")
+        mx = _load_file("ultra_rwka.components.kernels.mixer", os.path.join(pkg, "kernels", "mixer.py"),
+                        "ultra_rwka.components.kernels")
     finally:
         torch.jit.script = real_script
         if not had_warnings:
@@ -90,7 +96,7 @@ def load_reference(ref_root: str, ref_kernel):
                "ultra_rwka.components")
     tm = _load_file("ultra_rwka.components.attention.tm_kla", os.path.join(pkg, "attention", "tm_kla.py"),
                     "ultra_rwka.components.attention")
-    return fm.LearnablePositiveMap, tm.TMLinKernelAttn
+    return fm, mx, tm
 
 
 def gen(shape, seed, kind="normal", lo=0.0, hi=1.0):
