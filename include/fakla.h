@@ -125,6 +125,74 @@ int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
               void* out, int64_t rows, int64_t in_dim, int64_t feat_dim,
               int64_t heads, int dtype, void* stream);
 
+/*
+ * fakla_attention_backward -- gradients of fakla_attention.
+ *
+ * Reference: none -- the reference's FA-KLA has no backward (its gradient
+ * test, tests/backend/test_fa_kla_gradients.py, is empty). This is the
+ * derivative of the recurrence of cpu_kernels.cpp:107-164 (see fakla.h top):
+ * with dnum_t = dout_t / den_t, dden_t = -(q_t^T S_t dout_t) / den_t^2 and
+ * G_s = dS_final + sum_{t>=s} q_t dnum_t^T, g_s = dz_final + sum_{t>=s} q_t dden_t:
+ *   dq_t = S_t dnum_t + z_t dden_t,  dk~_s = G_s v_s + g_s,  dv_s = G_s^T k~_s,
+ *   dk_s = dk~_s temp_s,  dtemp_s = dk~_s . k_s,  dS0 = G_0,  dz0 = g_0.
+ *
+ *   q_mapped, k_mapped, v, temp : the forward's inputs (temp may be NULL)
+ *   dout     : (B, T, H, Dv) gradient of the output
+ *   S0, z0   : the forward's initial state, or NULL for zero
+ *   dS_final, dz_final : gradient of the forward's final state, or NULL
+ *   dq, dk   : (B, T, H, Df) written   dv : (B, T, H, Dv) written
+ *   dtemp    : (B, T, H) written, or NULL     dS0, dz0 : written, or NULL
+ * Gradients have the activation dtype; all accumulation is fp32. Needs a
+ * workspace of fakla_attention_backward_workspace_bytes().
+ */
+int fakla_attention_backward(const void* q_mapped, const void* k_mapped, const void* v,
+                             const void* temp, const void* dout, const float* S0,
+                             const float* z0, const float* dS_final, const float* dz_final,
+                             void* dq, void* dk, void* dv, void* dtemp, float* dS0, float* dz0,
+                             int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv,
+                             int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fakla_attention_backward_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Df,
+                                                int64_t Dv, int dtype);
+
+/*
+ * fakla_phi_backward -- gradient of the elu+1 activation from its output:
+ * dpre = dphi * min(phi, 1)  (elu'(x) = 1 for x > 0, e^x = phi for x <= 0).
+ *
+ * Reference: none (no backward in the reference); the derivative of
+ * F.elu(x) + 1 at feature_maps.py:248.
+ *   phi, dphi, dpre : n elements each (dpre may alias dphi)
+ */
+int fakla_phi_backward(const void* phi, const void* dphi, void* dpre, int64_t n, int dtype,
+                       void* stream);
+
+/*
+ * fakla_activation_backward -- gradient of a fakla_feature_map activation
+ * from its pre-activation p = x W^T + bias: dpre = dy * act'(p); for
+ * FAKLA_ACT_COSSIN, dy is (rows, 2 * n) and
+ * dpre = scale * (cos p * dy[:, n + j] - sin p * dy[:, j]).
+ *
+ * Reference: none (no backward in the reference); derivatives of the
+ * activations listed at fakla_activation.
+ *   pre : (rows, n)   dy : (rows, n), or (rows, 2n) for COSSIN   dpre : (rows, n)
+ */
+int fakla_activation_backward(const void* pre, const void* dy, void* dpre, int64_t rows,
+                              int64_t n, int act, float scale, int dtype, void* stream);
+
+/*
+ * fakla_mix_features_backward -- gradients of fakla_mix_features.
+ * With w = softmax(logits) (rounded to dtype as in the forward):
+ *   dfeats[i] = w_i dout,  dlogits_i = w_i (dw_i - sum_j w_j dw_j),  dw_i = dout . feats[i]
+ *
+ * Reference: none (no backward in the reference); the derivative of
+ * KernelFeatureMixer's combination (mixer.py:134-150).
+ *   feats : (n_maps, rows, feat_dim)  logits : (rows, n_maps)  dout : (rows, feat_dim)
+ *   dfeats : like feats, or NULL      dlogits : like logits, or NULL
+ */
+int fakla_mix_features_backward(const void* feats, const void* logits, const void* dout,
+                                void* dfeats, void* dlogits, int64_t rows, int64_t n_maps,
+                                int64_t feat_dim, int dtype, void* stream);
+
 /* Output activation of fakla_feature_map. */
 typedef enum {
   FAKLA_ACT_ELU1 = 0,     /* elu(x) + 1                        (feature_maps.py:248) */

@@ -53,6 +53,12 @@ SIGNATURES = {
     "fakla_attention": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),
     "fakla_attention_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "fakla_phi": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
+    "fakla_attention_backward": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                        _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "fakla_attention_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
+    "fakla_phi_backward": (_int, [_p, _p, _p, _i64, _int, _p]),
+    "fakla_activation_backward": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_float, _int, _p]),
+    "fakla_mix_features_backward": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "fakla_feature_map": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, ctypes.c_float, _int, _p]),
     "fakla_mix_features": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "fakla_prefill": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),

@@ -124,6 +124,10 @@ def fa_kla_attention_with_state(q_mapped: torch.Tensor, k_mapped: torch.Tensor, 
     B, T, H, Df = q_mapped.shape
     Dv = v_reshaped.shape[3]
     _check_state(state, B, H, Df, Dv, dev)
+    if _needs_grad(q_mapped, k_mapped, v_reshaped, temp, *(state or ())) and B * T * H > 0:
+        S0, z0 = state if state is not None else (None, None)
+        out, S, z = _AttentionFn.apply(q_mapped, k_mapped, v_reshaped, temp, S0, z0)
+        return out, ((S, z) if return_state else None)
     out = torch.empty_like(v_reshaped)
     S, z, flags = _state_buffers(state, return_state, B, H, Df, Dv, dev)
     if B * T * H == 0:
@@ -163,6 +167,11 @@ def phi_map(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] 
         rows *= s
     _require(temp is None or temp.numel() == rows * heads, "temp must hold one value per (row, head)")
     dev = _check_device([x, weight, bias, temp], ["x", "weight", "bias", "temp"])
+    if _needs_grad(x, weight, bias, temp) and rows > 0:
+        out = _PhiFn.apply(x.reshape(rows, in_dim), weight, bias)
+        if temp is not None:
+            out = (out.reshape(rows, heads, feat // heads) * temp.reshape(rows, heads, 1)).reshape(rows, feat)
+        return out.reshape(*lead, feat)
     dt = x.dtype
     _require(all(t is None or t.dtype == dt for t in (weight, bias, temp)), "x, weight, bias, temp must share a dtype")
     code = _dtype_code(x)
@@ -209,6 +218,12 @@ def fa_kla_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: to
     _require(all(t is None or t.is_contiguous() for t in (q, k, v, weight, bias, temp)), "All inputs must be contiguous")
     code = _dtype_code(q)
     _check_state(state, B, H, M, Dv, dev)
+    if _needs_grad(q, k, v, weight, bias, temp, *(state or ())) and B * T > 0:
+        # differentiable form: phi(q), phi(k) kept for the backward, then the
+        # attention (temperature applied in the scan so that it gets a gradient)
+        pq = _PhiFn.apply(q.reshape(B * T, in_dim), weight, bias).reshape(B, T, H, M)
+        pk = _PhiFn.apply(k.reshape(B * T, in_dim), weight, bias).reshape(B, T, H, M)
+        return fa_kla_attention_with_state(pq, pk, v, temp, state, return_state)
     out = torch.empty(B, T, H, Dv, device=dev, dtype=dt)
     S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
     if B * T == 0:
@@ -408,6 +423,16 @@ def feature_map(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tens
     """
     _require(act in ACTIVATIONS, f"unknown activation {act!r}; choose from {sorted(ACTIVATIONS)}")
     _require(weight.dim() == 2, "weight must be (n_out, in_dim)")
+    if _needs_grad(x, weight, bias):
+        if act == "elu+1" and out is None:
+            return phi_map(x, weight, bias)
+        lead = x.shape[:-1]
+        y = _FeatureMapFn.apply(x.reshape(-1, x.shape[-1]), weight, bias, act, float(scale))
+        y = y.reshape(*lead, y.shape[-1])
+        if out is not None:
+            out.copy_(y.reshape(out.shape))
+            return out
+        return y
     n_out, in_dim = weight.shape
     _require(x.shape[-1] == in_dim, f"x last dim {x.shape[-1]} != in_dim {in_dim}")
     _require(bias is None or tuple(bias.shape) == (n_out,), "bias must be (n_out,)")
@@ -446,6 +471,12 @@ def mix_features(feats: torch.Tensor, logits: torch.Tensor, out: Optional[torch.
     dev = _check_device([feats, logits, out], ["feats", "logits", "out"])
     _require(logits.dtype == feats.dtype, "feats and logits must have the same dtype")
     code = _dtype_code(feats)
+    if _needs_grad(feats, logits) and rows > 0:
+        y = _MixFn.apply(feats.contiguous(), logits.contiguous())
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
     feats = feats.contiguous()
     logits = logits.contiguous()
     if out is None:
@@ -456,3 +487,160 @@ def mix_features(feats: torch.Tensor, logits: torch.Tensor, out: Optional[torch.
     with torch.cuda.device(dev):
         _lib.check(L.fakla_mix_features(_ptr(feats), _ptr(logits), _ptr(out), rows, n_maps, F, code, _stream(dev)))
     return out
+
+
+# ----------------------------------------------------------------------------- autograd
+def _needs_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+class _AttentionFn(torch.autograd.Function):
+    """FA-KLA with gradients: forward fakla_attention (final state always
+    returned), backward fakla_attention_backward. The reference has no
+    backward; this differentiates its recurrence (cpu_kernels.cpp:107-164)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, temp, S0, z0):
+        ctx.set_materialize_grads(False)
+        B, T, H, Df = q.shape
+        Dv = v.shape[3]
+        dev = q.device
+        out = torch.empty_like(v)
+        S = S0.detach().clone() if S0 is not None else torch.empty(B, H, Df, Dv, device=dev, dtype=torch.float32)
+        z = z0.detach().clone() if z0 is not None else torch.empty(B, H, Df, device=dev, dtype=torch.float32)
+        flags = _lib.FAKLA_STATE_OUT | (_lib.FAKLA_STATE_IN if S0 is not None else 0)
+        L = _lib.lib()
+        code = _dtype_code(q)
+        with torch.cuda.device(dev):
+            ws_bytes = L.fakla_attention_workspace_bytes(B, T, H, Df, Dv, code)
+            ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+            _lib.check(L.fakla_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(temp), _ptr(out), _ptr(S), _ptr(z),
+                                         B, T, H, Df, Dv, code, flags, _ptr(ws), ws_bytes, _stream(dev)))
+        ctx.save_for_backward(q, k, v, temp, S0, z0)
+        return out, S, z
+
+    @staticmethod
+    def backward(ctx, dout, dS, dz):
+        q, k, v, temp, S0, z0 = ctx.saved_tensors
+        B, T, H, Df = q.shape
+        Dv = v.shape[3]
+        dev = q.device
+        if dout is None:
+            dout = torch.zeros_like(v)
+        dout = dout.contiguous().to(dtype=v.dtype)
+        if (dS is None) != (dz is None):
+            dS = torch.zeros(B, H, Df, Dv, device=dev) if dS is None else dS
+            dz = torch.zeros(B, H, Df, device=dev) if dz is None else dz
+        dS = None if dS is None else dS.contiguous().float()
+        dz = None if dz is None else dz.contiguous().float()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        dtemp = torch.empty_like(temp) if temp is not None and ctx.needs_input_grad[3] else None
+        want_state = S0 is not None and (ctx.needs_input_grad[4] or ctx.needs_input_grad[5])
+        dS0 = torch.empty_like(S0) if want_state else None
+        dz0 = torch.empty_like(z0) if want_state else None
+        L = _lib.lib()
+        code = _dtype_code(q)
+        with torch.cuda.device(dev):
+            ws_bytes = L.fakla_attention_backward_workspace_bytes(B, T, H, Df, Dv, code)
+            ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+            _lib.check(L.fakla_attention_backward(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(temp), _ptr(dout), _ptr(S0), _ptr(z0), _ptr(dS), _ptr(dz),
+                _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dtemp), _ptr(dS0), _ptr(dz0),
+                B, T, H, Df, Dv, code, _ptr(ws), ws_bytes, _stream(dev)))
+        return dq, dk, dv, dtemp, dS0, dz0
+
+
+class _PhiFn(torch.autograd.Function):
+    """phi(x) = elu(x W^T + b) + 1 with gradients: forward fakla_phi; backward
+    fakla_phi_backward (dpre = dphi * min(phi, 1)), then the two weight/input
+    GEMMs dx = dpre W, dW = dpre^T x (cuBLAS) and db = sum_rows dpre."""
+
+    @staticmethod
+    def forward(ctx, x, W, b):
+        rows, in_dim = x.shape
+        feat = W.shape[0]
+        dev = x.device
+        out = torch.empty(rows, feat, device=dev, dtype=x.dtype)
+        L = _lib.lib()
+        with torch.cuda.device(dev):
+            _lib.check(L.fakla_phi(_ptr(x), _ptr(W), _ptr(b), None, _ptr(out), rows, in_dim, feat, 1,
+                                   _dtype_code(x), _stream(dev)))
+        ctx.save_for_backward(x, W, out)
+        ctx.has_bias = b is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dphi):
+        x, W, phi = ctx.saved_tensors
+        dphi = dphi.contiguous().to(dtype=phi.dtype)
+        dpre = torch.empty_like(phi)
+        L = _lib.lib()
+        dev = phi.device
+        with torch.cuda.device(dev):
+            _lib.check(L.fakla_phi_backward(_ptr(phi), _ptr(dphi), _ptr(dpre), phi.numel(), _dtype_code(phi),
+                                            _stream(dev)))
+        dx = dpre @ W if ctx.needs_input_grad[0] else None
+        dW = dpre.t() @ x if ctx.needs_input_grad[1] else None
+        db = dpre.sum(0) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        return dx, dW, db
+
+
+class _FeatureMapFn(torch.autograd.Function):
+    """act(x W^T + b) with gradients for every fakla_feature_map activation:
+    the backward recomputes the pre-activation with one identity launch,
+    applies fakla_activation_backward, then dx = dpre W and dW = dpre^T x
+    (cuBLAS) and db = sum_rows dpre."""
+
+    @staticmethod
+    def forward(ctx, x, W, b, act, scale):
+        with torch.no_grad():
+            y = feature_map(x, W, b, act, scale)
+        ctx.save_for_backward(x, W, b)
+        ctx.act = act
+        ctx.scale = scale
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, W, b = ctx.saved_tensors
+        with torch.no_grad():
+            pre = feature_map(x, W, b, "identity")
+        dy = dy.contiguous().to(dtype=pre.dtype)
+        dpre = torch.empty_like(pre)
+        rows, n = pre.shape
+        L = _lib.lib()
+        dev = pre.device
+        with torch.cuda.device(dev):
+            _lib.check(L.fakla_activation_backward(_ptr(pre), _ptr(dy), _ptr(dpre), rows, n, ACTIVATIONS[ctx.act],
+                                                   ctx.scale, _dtype_code(pre), _stream(dev)))
+        dx = dpre @ W if ctx.needs_input_grad[0] else None
+        dW = dpre.t() @ x if ctx.needs_input_grad[1] else None
+        db = dpre.sum(0) if b is not None and ctx.needs_input_grad[2] else None
+        return dx, dW, db, None, None
+
+
+class _MixFn(torch.autograd.Function):
+    """KernelFeatureMixer combination with gradients (fakla_mix_features /
+    fakla_mix_features_backward)."""
+
+    @staticmethod
+    def forward(ctx, feats, logits):
+        with torch.no_grad():
+            y = mix_features(feats, logits)
+        ctx.save_for_backward(feats, logits)
+        return y
+
+    @staticmethod
+    def backward(ctx, dout):
+        feats, logits = ctx.saved_tensors
+        n_maps, rows, F = feats.shape
+        dout = dout.contiguous().to(dtype=feats.dtype)
+        dfeats = torch.empty_like(feats) if ctx.needs_input_grad[0] else None
+        dlogits = torch.empty_like(logits) if ctx.needs_input_grad[1] else None
+        L = _lib.lib()
+        dev = feats.device
+        with torch.cuda.device(dev):
+            _lib.check(L.fakla_mix_features_backward(_ptr(feats), _ptr(logits), _ptr(dout), _ptr(dfeats),
+                                                     _ptr(dlogits), rows, n_maps, F, _dtype_code(feats),
+                                                     _stream(dev)))
+        return dfeats, dlogits

@@ -307,6 +307,99 @@ extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const v
                  dtype, (cudaStream_t)stream, d);
 }
 
+extern "C" size_t fakla_attention_backward_workspace_bytes(int64_t B, int64_t T, int64_t H,
+                                                           int64_t Df, int64_t Dv, int dtype) {
+  (void)Df;
+  (void)Dv;
+  (void)dtype;
+  if (B < 1 || T < 1 || H < 1) return 0;
+  return round_up(fakla::backward_workspace_bytes(B, T, H), 256);
+}
+
+extern "C" int fakla_attention_backward(const void* q, const void* k, const void* v,
+                                        const void* temp, const void* dout, const float* S0,
+                                        const float* z0, const float* dS_final,
+                                        const float* dz_final, void* dq, void* dk, void* dv,
+                                        void* dtemp, float* dS0, float* dz0, int64_t B, int64_t T,
+                                        int64_t H, int64_t Df, int64_t Dv, int dtype,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !dout || !dq || !dk || !dv)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "q, k, v, dout, dq, dk and dv must be non-NULL");
+  if (B < 1 || T < 1 || H < 1 || Df < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if ((S0 == nullptr) != (z0 == nullptr) || (dS_final == nullptr) != (dz_final == nullptr) ||
+      (dS0 == nullptr) != (dz0 == nullptr))
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG,
+                           "S0/z0, dS_final/dz_final and dS0/dz0 must each be both NULL or both non-NULL");
+  if (!fakla::backward_simt_supported(Df, Dv))
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "backward head dims Df=%lld Dv=%lld unsupported",
+                           (long long)Df, (long long)Dv);
+  const size_t need = fakla_attention_backward_workspace_bytes(B, T, H, Df, Dv, dtype);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fakla_set_error(FAKLA_ERR_WORKSPACE, "backward needs %zu workspace bytes, got %zu", need,
+                           workspace == nullptr ? (size_t)0 : workspace_bytes);
+  if (((uintptr_t)workspace & 3u) != 0)
+    return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 4-byte aligned");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_backward_simt(dtype, q, k, v, temp, dout, S0, z0, dS_final,
+                                              dz_final, dq, dk, dv, dtemp, dS0, dz0, B, T, H, Df,
+                                              Dv, workspace, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "attention backward launch");
+  return FAKLA_OK;
+}
+
+extern "C" int fakla_phi_backward(const void* phi, const void* dphi, void* dpre, int64_t n,
+                                  int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!phi || !dphi || !dpre) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "NULL pointer");
+  if (n < 1) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "n must be positive");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_phi_backward(dtype, phi, dphi, dpre, n, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "phi backward launch");
+  return FAKLA_OK;
+}
+
+extern "C" int fakla_activation_backward(const void* pre, const void* dy, void* dpre, int64_t rows,
+                                         int64_t n, int act, float scale, int dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!pre || !dy || !dpre) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "NULL pointer");
+  if (act < FAKLA_ACT_ELU1 || act > FAKLA_ACT_COSSIN)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "unknown activation %d", act);
+  if (rows < 1 || n < 1) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_activation_backward(dtype, act, pre, dy, dpre, rows, n, scale,
+                                                    (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "activation backward launch");
+  return FAKLA_OK;
+}
+
+extern "C" int fakla_mix_features_backward(const void* feats, const void* logits, const void* dout,
+                                           void* dfeats, void* dlogits, int64_t rows,
+                                           int64_t n_maps, int64_t feat_dim, int dtype,
+                                           void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!feats || !logits || !dout) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "NULL pointer");
+  if (rows < 1 || n_maps < 1 || feat_dim < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if (!fakla::mix_supported(n_maps))
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "at most 32 feature maps can be mixed, got %lld",
+                           (long long)n_maps);
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaError_t e = fakla::launch_mix_backward(dtype, feats, logits, dout, dfeats, dlogits, rows,
+                                             n_maps, feat_dim, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "mix backward launch");
+  return FAKLA_OK;
+}
+
 extern "C" int fakla_feature_map(const void* x, const void* W, const void* bias, void* out,
                                  int64_t rows, int64_t in_dim, int64_t n_out, int act, float scale,
                                  int dtype, void* stream) {

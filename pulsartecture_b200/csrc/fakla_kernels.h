@@ -32,6 +32,24 @@ cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v
                           const void* temp, void* out, float* S, float* z, int64_t NH,
                           int64_t Df, int64_t Dv, cudaStream_t stream);
 
+// Backward on CUDA cores (simt_backward.cu).
+bool backward_simt_supported(int64_t Df, int64_t Dv);
+size_t backward_workspace_bytes(int64_t B, int64_t T, int64_t H);
+cudaError_t launch_backward_simt(int dtype, const void* q, const void* k, const void* v,
+                                 const void* temp, const void* dout, const float* S0,
+                                 const float* z0, const float* dS_final, const float* dz_final,
+                                 void* dq, void* dk, void* dv, void* dtemp, float* dS0, float* dz0,
+                                 int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv,
+                                 void* workspace, cudaStream_t stream);
+cudaError_t launch_phi_backward(int dtype, const void* phi, const void* dphi, void* dpre,
+                                int64_t n, cudaStream_t stream);
+cudaError_t launch_activation_backward(int dtype, int act, const void* pre, const void* dy,
+                                       void* dpre, int64_t rows, int64_t n, float scale,
+                                       cudaStream_t stream);
+cudaError_t launch_mix_backward(int dtype, const void* feats, const void* logits, const void* dout,
+                                void* dfeats, void* dlogits, int64_t rows, int64_t n_maps,
+                                int64_t F, cudaStream_t stream);
+
 // Tensor-core kernels (sm100_phi.cu, sm100_scan.cu); bf16 only.
 bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads);
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,

@@ -411,6 +411,160 @@ static cudaError_t launch_mix_t(const void* feats, const void* logits, void* out
 
 bool mix_supported(int64_t n_maps) { return n_maps >= 1 && n_maps <= kMaxMaps; }
 
+// d(elu(x) + 1)/dx from the output phi: 1 where phi > 1 (x > 0), phi otherwise.
+template <typename T>
+__global__ void phi_backward_kernel(const T* __restrict__ phi, const T* __restrict__ dphi,
+                                    T* __restrict__ dpre, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float p = to_f32(phi[i]);
+    dpre[i] = from_f32<T>(to_f32(dphi[i]) * (p > 1.f ? 1.f : p));
+  }
+}
+
+// Derivatives of the fakla_feature_map activations at the pre-activation x.
+template <int ACT>
+__device__ __forceinline__ float activation_grad(float x) {
+  if constexpr (ACT == FAKLA_ACT_ELU1) {
+    return x > 0.f ? 1.f : expf(x);
+  } else if constexpr (ACT == FAKLA_ACT_RELU) {
+    return x > 0.f ? 1.f : 0.f;
+  } else if constexpr (ACT == FAKLA_ACT_SOFTPLUS) {
+    return x > 20.f ? 1.f : 1.f / (1.f + expf(-x));
+  } else if constexpr (ACT == FAKLA_ACT_GELU) {
+    return 0.5f * (1.f + erff(x * 0.70710678118654752f)) + x * 0.3989422804014327f * expf(-0.5f * x * x);
+  } else if constexpr (ACT == FAKLA_ACT_SIGMOID) {
+    const float sg = 1.f / (1.f + expf(-x));
+    return sg * (1.f - sg);
+  } else if constexpr (ACT == FAKLA_ACT_ABS) {
+    return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+  } else {
+    return 1.f;  // FAKLA_ACT_IDENTITY
+  }
+}
+
+template <typename T, int ACT>
+__global__ void activation_backward_kernel(const T* __restrict__ pre, const T* __restrict__ dy,
+                                           T* __restrict__ dpre, int64_t rows, int64_t n,
+                                           float scale) {
+  const int64_t total = rows * n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = to_f32(pre[i]);
+    if constexpr (ACT == FAKLA_ACT_COSSIN) {
+      const int64_t r = i / n, c = i % n;
+      float sn, cs;
+      sincosf(x, &sn, &cs);
+      dpre[i] = from_f32<T>(scale * (cs * to_f32(dy[r * 2 * n + n + c]) - sn * to_f32(dy[r * 2 * n + c])));
+    } else {
+      dpre[i] = from_f32<T>(to_f32(dy[i]) * activation_grad<ACT>(x));
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t launch_act_bwd_t(int act, const void* pre, const void* dy, void* dpre,
+                                    int64_t rows, int64_t n, float scale, cudaStream_t stream) {
+  const int64_t want = (rows * n + 255) / 256;
+  const unsigned grid = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+#define FAKLA_ACTB_CASE(A)                                                                 \
+  case A:                                                                                  \
+    activation_backward_kernel<T, A><<<grid, 256, 0, stream>>>((const T*)pre, (const T*)dy, \
+                                                               (T*)dpre, rows, n, scale); \
+    break;
+  switch (act) {
+    FAKLA_ACTB_CASE(FAKLA_ACT_ELU1)
+    FAKLA_ACTB_CASE(FAKLA_ACT_RELU)
+    FAKLA_ACTB_CASE(FAKLA_ACT_SOFTPLUS)
+    FAKLA_ACTB_CASE(FAKLA_ACT_GELU)
+    FAKLA_ACTB_CASE(FAKLA_ACT_IDENTITY)
+    FAKLA_ACTB_CASE(FAKLA_ACT_SIGMOID)
+    FAKLA_ACTB_CASE(FAKLA_ACT_ABS)
+    FAKLA_ACTB_CASE(FAKLA_ACT_COSSIN)
+    default: return cudaErrorInvalidValue;
+  }
+#undef FAKLA_ACTB_CASE
+  return cudaGetLastError();
+}
+
+cudaError_t launch_activation_backward(int dtype, int act, const void* pre, const void* dy,
+                                       void* dpre, int64_t rows, int64_t n, float scale,
+                                       cudaStream_t stream) {
+  if (dtype == FAKLA_BF16)
+    return launch_act_bwd_t<__nv_bfloat16>(act, pre, dy, dpre, rows, n, scale, stream);
+  return launch_act_bwd_t<float>(act, pre, dy, dpre, rows, n, scale, stream);
+}
+
+// Mixer backward: one warp per row. w = softmax(logits) rounded to T as in
+// the forward; dw_i = dout . feats[i]; dlogits_i = w_i (dw_i - sum_j w_j dw_j);
+// dfeats[i] = w_i dout.
+template <typename T>
+__global__ void mix_backward_kernel(const T* __restrict__ feats, const T* __restrict__ logits,
+                                    const T* __restrict__ dout, T* __restrict__ dfeats,
+                                    T* __restrict__ dlogits, int64_t rows, int n_maps, int64_t F) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float w[kMaxMaps], dw[kMaxMaps];
+  float mx = -INFINITY;
+  for (int i = 0; i < n_maps; ++i) {
+    w[i] = to_f32(logits[r * n_maps + i]);
+    mx = fmaxf(mx, w[i]);
+  }
+  float den = 0.f;
+  for (int i = 0; i < n_maps; ++i) {
+    w[i] = expf(w[i] - mx);
+    den += w[i];
+  }
+  for (int i = 0; i < n_maps; ++i) {
+    w[i] = to_f32(from_f32<T>(w[i] / den));
+    dw[i] = 0.f;
+  }
+  for (int64_t c = lane; c < F; c += 32) {
+    const float g = to_f32(dout[r * F + c]);
+    for (int i = 0; i < n_maps; ++i) {
+      const int64_t idx = ((int64_t)i * rows + r) * F + c;
+      dw[i] = fmaf(g, to_f32(feats[idx]), dw[i]);
+      if (dfeats) dfeats[idx] = from_f32<T>(w[i] * g);
+    }
+  }
+  for (int i = 0; i < n_maps; ++i)
+    for (int o = 16; o > 0; o >>= 1) dw[i] += __shfl_xor_sync(0xffffffffu, dw[i], o);
+  if (dlogits && lane == 0) {
+    float s = 0.f;
+    for (int i = 0; i < n_maps; ++i) s += w[i] * dw[i];
+    for (int i = 0; i < n_maps; ++i) dlogits[r * n_maps + i] = from_f32<T>(w[i] * (dw[i] - s));
+  }
+}
+
+cudaError_t launch_mix_backward(int dtype, const void* feats, const void* logits, const void* dout,
+                                void* dfeats, void* dlogits, int64_t rows, int64_t n_maps,
+                                int64_t F, cudaStream_t stream) {
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (dtype == FAKLA_BF16)
+    mix_backward_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)feats, (const __nv_bfloat16*)logits, (const __nv_bfloat16*)dout,
+        (__nv_bfloat16*)dfeats, (__nv_bfloat16*)dlogits, rows, (int)n_maps, F);
+  else
+    mix_backward_kernel<float><<<grid, 256, 0, stream>>>((const float*)feats, (const float*)logits,
+                                                         (const float*)dout, (float*)dfeats,
+                                                         (float*)dlogits, rows, (int)n_maps, F);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_phi_backward(int dtype, const void* phi, const void* dphi, void* dpre,
+                                int64_t n, cudaStream_t stream) {
+  const int64_t want = (n + 255) / 256;
+  const unsigned grid = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+  if (dtype == FAKLA_BF16)
+    phi_backward_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)phi, (const __nv_bfloat16*)dphi, (__nv_bfloat16*)dpre, n);
+  else
+    phi_backward_kernel<float><<<grid, 256, 0, stream>>>((const float*)phi, (const float*)dphi,
+                                                         (float*)dpre, n);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_mix_features(int dtype, const void* feats, const void* logits, void* out,
                                 int64_t rows, int64_t n_maps, int64_t F, cudaStream_t stream) {
   if (dtype == FAKLA_BF16) return launch_mix_t<__nv_bfloat16>(feats, logits, out, rows, n_maps, F, stream);

@@ -136,11 +136,17 @@ class RandomFourierFeatures(FeatureMap):
             x = x.to(device=self.W.device, dtype=self.W.dtype)
         return x
 
+    def _w_rows(self) -> torch.Tensor:
+        # under autograd a learnable W must stay in the graph: transpose it there
+        if torch.is_grad_enabled() and self.W.requires_grad:
+            return self.W.t().contiguous()
+        return self._wt.get(self.W)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return feature_map(self._prep(x), self._wt.get(self.W), self.b, "cossin", self.scale_factor)
+        return feature_map(self._prep(x), self._w_rows(), self.b, "cossin", self.scale_factor)
 
     def forward_into(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        return feature_map(self._prep(x), self._wt.get(self.W), self.b, "cossin", self.scale_factor, out=out)
+        return feature_map(self._prep(x), self._w_rows(), self.b, "cossin", self.scale_factor, out=out)
 
     def extra_repr(self) -> str:
         return f"{super().extra_repr()}, gamma={self.gamma}, learnable={self.learnable}"

@@ -124,9 +124,13 @@ class KernelFeatureMixer(nn.Module):
         # our maps compute in the dtype of their parameters / buffers.
         first = self.feature_maps[0]
         ref = next(iter(list(first.parameters()) + list(first.buffers())), x)
-        feats = torch.empty(self.num_feature_maps, rows, self.feature_dim, device=x.device, dtype=ref.dtype)
-        for i, fm in enumerate(self.feature_maps):
-            fm.forward_into(x2, feats[i])
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            # autograd: each map's output stays a graph node
+            feats = torch.stack([fm(x2).to(dtype=ref.dtype) for fm in self.feature_maps])
+        else:
+            feats = torch.empty(self.num_feature_maps, rows, self.feature_dim, device=x.device, dtype=ref.dtype)
+            for i, fm in enumerate(self.feature_maps):
+                fm.forward_into(x2, feats[i])
         mixed = mix_features(feats, logits.reshape(rows, -1).to(dtype=feats.dtype))
         return mixed.reshape(*lead, self.feature_dim)
 
