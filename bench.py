@@ -239,8 +239,9 @@ def workload_config(world):
 def run_only(args):
     """One kernel of the path alone, on the benchmark's shapes: `phi` = the
     phi GEMM for q and k of config 2 (2*65536 rows), `scan` = the chunk scan of
-    config 2 on precomputed phi, `decode` = the decode state kernel of config 4.
-    Prints the mean device time per launch."""
+    config 2 on precomputed phi, `decode` = the decode state kernel of config 4,
+    `backward` = the attention backward (both sweeps) on config 2's mapped
+    shapes. Prints the mean device time per launch."""
     from pulsartecture_b200 import _lib
 
     dev = torch.device("cuda", 0)
@@ -270,6 +271,21 @@ def run_only(args):
                                              out.data_ptr(), S.data_ptr(), z.data_ptr(), B, T, H, D, D,
                                              _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, None, 0, sh))
             fn = scan
+    elif args.only == "backward":
+        qm = (torch.rand(B, T, H, D, generator=g, device=dev) + 0.5).bfloat16()
+        km = (torch.rand(B, T, H, D, generator=g, device=dev) + 0.5).bfloat16()
+        v = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+        do = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+        dq, dk, dv = torch.empty_like(qm), torch.empty_like(km), torch.empty_like(v)
+        wsb = L.fakla_attention_backward_workspace_bytes(B, T, H, D, D, _lib.FAKLA_BF16)
+        ws = torch.empty(wsb, device=dev, dtype=torch.uint8)
+
+        def bwd():
+            _lib.check(L.fakla_attention_backward(qm.data_ptr(), km.data_ptr(), v.data_ptr(), None, do.data_ptr(),
+                                                  None, None, None, None, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                                  None, None, None, B, T, H, D, D, _lib.FAKLA_BF16, ws.data_ptr(), wsb,
+                                                  sh))
+        fn = bwd
     else:
         S = torch.randn(DEC_N, DEC_H, D, D, generator=g, device=dev) * 0.02
         z = torch.rand(DEC_N, DEC_H, D, generator=g, device=dev) + 0.5
@@ -372,7 +388,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode", "sustained"],
+    ap.add_argument("--no-module", action="store_true")
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -544,6 +561,48 @@ def main():
         }
         del Sd, zd, qd, kd, vd, dwsb
 
+    # ---- module forward (TMLinKernelAttn, embed 2048 -> 16 heads of 128, bf16, inference):
+    # projections folded into the feature map (one GEMM + scan) against the
+    # projections as three library GEMMs followed by the fused prefill
+    module = None
+    if not args.no_module:
+        from pulsartecture_b200.attention import TMLinKernelAttn
+        from pulsartecture_b200.backend.interface import fa_kla_prefill
+        from pulsartecture_b200.kernels import LearnablePositiveMap
+
+        torch.manual_seed(0)
+        mod = TMLinKernelAttn(IN_DIM, LearnablePositiveMap(IN_DIM, H * D, dtype=torch.bfloat16), num_heads=H,
+                              qk_dim=D, v_dim=D, dtype=torch.bfloat16).to(dev).eval()
+        gm = torch.Generator(device=dev).manual_seed(3000 + rank)
+        xm = (torch.randn(B, T, IN_DIM, generator=gm, device=dev) * 0.5).bfloat16()
+        with torch.no_grad():
+            assert mod._qkv_foldable(xm)
+
+            def folded():
+                mod(xm)
+
+            def unfolded():
+                qp, kp, vp = mod.proj_q(xm), mod.proj_k(xm), mod.proj_v(xm)
+                fa_kla_prefill(qp, kp, vp.reshape(B, T, H, D), mod.feature_mapper.weight, mod.feature_mapper.bias,
+                               None, None, False)
+
+            for fn in (folded, unfolded):
+                for _ in range(3):
+                    fn()
+            torch.cuda.synchronize()
+            m_steps = max(5, min(args.steps, 20))
+            f_ms = time_loop(folded, m_steps, stream) / m_steps
+            u_ms = time_loop(unfolded, m_steps, stream) / m_steps
+        module = {
+            "workload": "TMLinKernelAttn forward (inference): x (8, 4096, 2048) bf16 -> 16 heads of 128, "
+                        "LearnablePositiveMap(2048 -> 2048) fused",
+            "folded_ms": f_ms, "folded_tokens_per_s": B * T / (f_ms * 1e-3),
+            "unfolded_ms": u_ms, "unfolded_tokens_per_s": B * T / (u_ms * 1e-3),
+            "note": "folded = projections folded into the feature map (fakla_qkv_prefill, one GEMM for "
+                    "[phi(q) | phi(k) | v] + scan); unfolded = three cuBLAS projections + fakla_prefill",
+        }
+        del mod, xm
+
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -575,6 +634,7 @@ def main():
             },
             "e2e": e2e,
             "decode": decode,
+            "module_forward": module,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": 2 * args.steps,

@@ -271,6 +271,33 @@ size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim,
                                      int64_t H, int64_t M, int64_t Dv, int dtype);
 
 /*
+ * fakla_qkv_prefill -- the projections, the feature map and FA-KLA from the
+ * layer input: TMLinKernelAttn.forward (ultra_rwka/attention/tm_kla.py:
+ * 255-332) with q = x Wq^T + bq, k = x Wk^T + bk, v = x Wv^T + bv and
+ * phi(y) = elu(y Wphi^T + bphi) + 1, the projections folded into the map:
+ *   phi(q) = elu(x (Wphi Wq)^T + (Wphi bq + bphi)) + 1   (same for k).
+ * One GEMM computes [phi(q) | phi(k) * temp | v] for every row of x, and the
+ * scan reads those column blocks in place.
+ *
+ *   x    : (B, T, embed)
+ *   W    : (2*H*M + H*Dv, embed) = [Wphi Wq ; Wphi Wk ; Wv]   (row blocks)
+ *   bias : (2*H*M + H*Dv) = [Wphi bq + bphi ; Wphi bk + bphi ; bv], or NULL
+ *   temp : (B, T, H) or NULL     out : (B, T, H, Dv)
+ *   S, z, flags : as fakla_attention, with Df = M.
+ * Implemented for BF16 with M = Dv = 128, embed % 64 == 0, (2*H*M + H*Dv) %
+ * 256 == 0, 16-byte aligned pointers; other cases return FAKLA_ERR_UNSUPPORTED.
+ * Workspace: fakla_qkv_prefill_workspace_bytes() (the GEMM output, then the
+ * scan's optional segment records).
+ */
+int fakla_qkv_prefill(const void* x, const void* W, const void* bias, const void* temp,
+                      void* out, float* S, float* z, int64_t B, int64_t T, int64_t embed,
+                      int64_t H, int64_t M, int64_t Dv, int dtype, unsigned flags,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fakla_qkv_prefill_workspace_bytes(int64_t B, int64_t T, int64_t embed, int64_t H,
+                                         int64_t M, int64_t Dv, int dtype);
+
+/*
  * fakla_decode_mapped -- one recurrent step for N independent sequences on
  * already feature-mapped q, k. Reference: none (the reference is stateless,
  * tm_kla.py:229-337); this is the loop body of cpu_kernels.cpp:121-162 run on

@@ -63,6 +63,8 @@ SIGNATURES = {
     "fakla_mix_features": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "fakla_prefill": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),
     "fakla_prefill_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
+    "fakla_qkv_prefill": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _uint, _p, _sz, _p]),
+    "fakla_qkv_prefill_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
     "fakla_decode_mapped": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
     "fakla_decode": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _p, _sz, _p]),
     "fakla_decode_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),

@@ -27,8 +27,10 @@ from ..backend.interface import (
     State,
     fa_kla_attention_with_state,
     fa_kla_decode_step,
+    _needs_grad,
     fa_kla_prefill,
     fa_kla_prefill_host,
+    fa_kla_qkv_prefill,
     new_state,
 )
 from ..components.projections import LinearProjection
@@ -133,6 +135,47 @@ class TMLinKernelAttn(nn.Module):
         temp = self.temp_func(temp_input)
         return temp.to(dtype=dtype).contiguous()
 
+    # ------------------------------------------------------------- q/k/v folded into phi
+    def _qkv_foldable(self, x: torch.Tensor) -> bool:
+        """Inference with the default map on plain linear projections: the
+        projections can be folded into the feature map (fakla_qkv_prefill)."""
+        mapper = self.feature_mapper
+        if not (isinstance(mapper, LearnablePositiveMap) and mapper.fusable):
+            return False
+        projs = (self.proj_q, self.proj_k, self.proj_v)
+        if any(p.norm is not None or p.activation is not None for p in projs):
+            return False
+        if self.training and not isinstance(self.dropout, nn.Identity):
+            return False
+        if _needs_grad(x, *self.parameters()):
+            return False
+        dt = mapper.weight.dtype
+        H, M, Dv = self.num_heads, self.feature_dim // self.num_heads, self.v_head_dim
+        return (x.is_cuda and dt == torch.bfloat16 and M == 128 and Dv == 128 and self.embed_dim % 64 == 0
+                and (2 * H * M + H * Dv) % 256 == 0 and self.feature_dim % self.num_heads == 0)
+
+    def _qkv_fold(self):
+        """[Wphi Wq; Wphi Wk; Wv] and [Wphi bq + bphi; Wphi bk + bphi; bv], computed
+        in fp32 and cached until a parameter changes."""
+        mapper = self.feature_mapper
+        params = (self.proj_q.linear.weight, self.proj_q.linear.bias, self.proj_k.linear.weight,
+                  self.proj_k.linear.bias, self.proj_v.linear.weight, self.proj_v.linear.bias,
+                  mapper.weight, mapper.bias)
+        key = tuple(None if p is None else (p.data_ptr(), p._version) for p in params) + (mapper.weight.dtype,)
+        if getattr(self, "_fold_key", None) != key:
+            with torch.no_grad():
+                wq, bq, wk, bk, wv, bv, wp, bp = [None if p is None else p.float() for p in params]
+                zero = lambda n: torch.zeros(n, device=wp.device)  # noqa: E731
+                bq = zero(wq.shape[0]) if bq is None else bq
+                bk = zero(wk.shape[0]) if bk is None else bk
+                bv = zero(wv.shape[0]) if bv is None else bv
+                bp = zero(wp.shape[0]) if bp is None else bp
+                W = torch.cat([wp @ wq, wp @ wk, wv]).to(mapper.weight.dtype).contiguous()
+                b = torch.cat([wp @ bq + bp, wp @ bk + bp, bv]).to(mapper.weight.dtype).contiguous()
+            self._fold = (W, b)
+            self._fold_key = key
+        return self._fold
+
     def forward(self, x: torch.Tensor, temp_input: Optional[torch.Tensor] = None,
                 mixer_context: Optional[torch.Tensor] = None, state: Optional[State] = None,
                 return_state: bool = False):
@@ -141,6 +184,13 @@ class TMLinKernelAttn(nn.Module):
             x = x.contiguous()
         B, T, _ = x.shape
         H, Dv = self.num_heads, self.v_head_dim
+        if self._qkv_foldable(x):
+            W, b = self._qkv_fold()
+            temp = self._temperature(B, T, temp_input, W.dtype)
+            out, st = fa_kla_qkv_prefill(self.dropout(x).to(W.dtype), W, b, H, self.feature_dim // H, Dv, temp,
+                                         state, return_state)
+            out = out.reshape(B, T, self.total_v_dim)
+            return (out, st) if return_state else out
         x = self.dropout(x)
         q_proj = self.proj_q(x)
         k_proj = self.proj_k(x)

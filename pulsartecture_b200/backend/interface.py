@@ -644,3 +644,39 @@ class _MixFn(torch.autograd.Function):
                                                      _ptr(dlogits), rows, n_maps, F, _dtype_code(feats),
                                                      _stream(dev)))
         return dfeats, dlogits
+
+
+def fa_kla_qkv_prefill(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], H: int, M: int, Dv: int,
+                       temp: Optional[torch.Tensor] = None, state: Optional[State] = None,
+                       return_state: bool = True):
+    """Projections folded into the feature map, then FA-KLA (fakla_qkv_prefill).
+
+    x: (B, T, embed); weight: (2*H*M + H*Dv, embed) = [Wphi Wq; Wphi Wk; Wv];
+    bias: (2*H*M + H*Dv,) or None; temp: (B, T, H) or None. Forward only.
+    Returns (out (B, T, H, Dv), (S, z) or None).
+    """
+    _require(x.dim() == 3, "x must be (B, T, embed)")
+    B, T, E = x.shape
+    N = 2 * H * M + H * Dv
+    _require(tuple(weight.shape) == (N, E), f"weight must be ({N}, {E})")
+    _require(bias is None or tuple(bias.shape) == (N,), f"bias must be ({N},)")
+    _require(temp is None or tuple(temp.shape) == (B, T, H), "temp must be (B, T, H)")
+    dev = _check_device([x, weight, bias, temp], ["x", "weight", "bias", "temp"])
+    dt = x.dtype
+    _require(all(t is None or t.dtype == dt for t in (weight, bias, temp)), "All inputs must have the same dtype")
+    x, weight = x.contiguous(), weight.contiguous()
+    bias = None if bias is None else bias.contiguous()
+    temp = None if temp is None else temp.contiguous()
+    code = _dtype_code(x)
+    _check_state(state, B, H, M, Dv, dev)
+    out = torch.empty(B, T, H, Dv, device=dev, dtype=dt)
+    S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
+    if B * T == 0:
+        return out, ((S, z) if return_state else None)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        ws_bytes = L.fakla_qkv_prefill_workspace_bytes(B, T, E, H, M, Dv, code)
+        ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
+        _lib.check(L.fakla_qkv_prefill(_ptr(x), _ptr(weight), _ptr(bias), _ptr(temp), _ptr(out), _ptr(S), _ptr(z),
+                                       B, T, E, H, M, Dv, code, flags, _ptr(ws), ws_bytes, _stream(dev)))
+    return out, ((S, z) if return_state else None)

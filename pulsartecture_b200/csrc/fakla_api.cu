@@ -484,6 +484,64 @@ extern "C" int fakla_prefill(const void* q, const void* k, const void* v, const 
                        ws + 2 * one, workspace_bytes - 2 * one, st, d);
 }
 
+static size_t qkv_buffer_bytes(int64_t B, int64_t T, int64_t H, int64_t M, int64_t Dv) {
+  return round_up((size_t)B * (size_t)T * (size_t)(2 * H * M + H * Dv) * 2, 256);
+}
+
+extern "C" size_t fakla_qkv_prefill_workspace_bytes(int64_t B, int64_t T, int64_t embed, int64_t H,
+                                                    int64_t M, int64_t Dv, int dtype) {
+  (void)embed;
+  if (B < 1 || T < 1 || H < 1 || M < 1 || Dv < 1 || dtype != FAKLA_BF16) return 0;
+  return qkv_buffer_bytes(B, T, H, M, Dv) + scan_workspace(B, T, H, M, Dv, dtype);
+}
+
+extern "C" int fakla_qkv_prefill(const void* x, const void* W, const void* bias, const void* temp,
+                                 void* out, float* S, float* z, int64_t B, int64_t T,
+                                 int64_t embed, int64_t H, int64_t M, int64_t Dv, int dtype,
+                                 unsigned flags, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!x || !W || !out) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "x, W and out must be non-NULL");
+  if (B < 1 || T < 1 || embed < 1 || H < 1 || M < 1 || Dv < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if ((rc = check_state(S, z, flags))) return rc;
+  const int64_t rows = B * T;
+  if (dtype != FAKLA_BF16 || M != 128 || Dv != 128 ||
+      !fakla::qkv_sm100_supported(rows, embed, H * M, H * Dv, H) ||
+      !fakla::scan_sm100_supported(B, T, H, M, Dv))
+    return fakla_set_error(FAKLA_ERR_UNSUPPORTED,
+                           "fakla_qkv_prefill serves bf16, M = Dv = 128, embed %% 64 == 0 (got dtype=%d M=%lld "
+                           "Dv=%lld embed=%lld)", dtype, (long long)M, (long long)Dv, (long long)embed);
+  if (!aligned16(x) || !aligned16(W) || !aligned16(out) || (bias && !aligned16(bias)) ||
+      (S && !aligned16(S)))
+    return fakla_set_error(FAKLA_ERR_ALIGNMENT, "x, W, bias, out and S must be 16-byte aligned");
+  const size_t need = qkv_buffer_bytes(B, T, H, M, Dv);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fakla_set_error(FAKLA_ERR_WORKSPACE, "qkv prefill needs at least %zu workspace bytes, got %zu",
+                           need, workspace == nullptr ? (size_t)0 : workspace_bytes);
+  if (!aligned16(workspace))
+    return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* buf = (uint8_t*)workspace;
+  bool enc = false;
+  cudaError_t e = fakla::launch_qkv_sm100(x, W, bias, temp, buf, rows, embed, H * M, H * Dv, H, st,
+                                          d->status, &enc);
+  if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+  if (e != cudaSuccess) return cuda_fail(e, "qkv GEMM launch");
+  const int64_t row_elems = 2 * H * M + H * Dv;
+  const void* phq = buf;
+  const void* phk = buf + (size_t)H * M * 2;
+  const void* vv = buf + (size_t)2 * H * M * 2;
+  e = fakla::launch_scan_sm100(phq, phk, vv, nullptr, out, S, z, B, T, H, flags, buf + need,
+                               workspace_bytes - need, d->sms, st, d->status, &enc, row_elems);
+  if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+  if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
+  return FAKLA_OK;
+}
+
 extern "C" int fakla_decode_mapped(const void* q, const void* k, const void* v, const void* temp,
                                    void* out, float* S, float* z, int64_t N, int64_t H,
                                    int64_t Df, int64_t Dv, int dtype, void* stream) {

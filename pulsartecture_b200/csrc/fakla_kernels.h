@@ -66,6 +66,13 @@ size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms);
 cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
-                              cudaStream_t stream, int* status, bool* encoded);
+                              cudaStream_t stream, int* status, bool* encoded,
+                              int64_t in_row_elems = 0);
+// q/k/v GEMM: out (rows, 2*feat + vdim) = [phi(q) | phi(k) * temp | v] from
+// x (rows, K) and W (2*feat + vdim, K).
+bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads);
+cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, const void* temp,
+                             void* out, int64_t rows, int64_t K, int64_t feat, int64_t vdim,
+                             int64_t heads, cudaStream_t stream, int* status, bool* encoded);
 
 }  // namespace fakla

@@ -59,6 +59,9 @@ struct PhiArgs {
   const __nv_bfloat16* temp0;  // [rows, heads] or null (row set 0)
   const __nv_bfloat16* temp1;  // [rows, heads] or null (row set 1)
   int rows, N, K, heads, nsets;
+  int m;                       // features per head (temperature index = (col - tcol0) / m)
+  int ident_from;              // columns >= ident_from skip the activation (N: none)
+  int tcol0, tcol1;            // temperature applies to columns [tcol0, tcol1)
   int* status;
 };
 
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const int ew = warp - 2;         // epilogue warp index (staging buffer owner)
     const int half = ew >> 2;        // which 128 of the tile's 256 columns
     uint8_t* buf = sOut + ew * kOutWarpBytes;
-    const int m = args.N / args.heads;  // features per head
+    const int m = args.m;  // features per head
     int acc = 0;
     uint32_t acc_phase = 0;
     bool stored = false;
@@ -232,9 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           if (lane == 0) mbar_arrive(&tempty[acc]);
         }
         const int c0 = col0 + j * 64;
+        const bool ident = c0 >= args.ident_from;  // identity columns (the v block of a q/k/v GEMM)
         float tscale = 1.f;
-        if (temp != nullptr && grow < args.rows)
-          tscale = __bfloat162float(temp[(int64_t)grow * args.heads + c0 / m]);
+        if (temp != nullptr && grow < args.rows && c0 >= args.tcol0 && c0 < args.tcol1)
+          tscale = __bfloat162float(temp[(int64_t)grow * args.heads + (c0 - args.tcol0) / m]);
         uint32_t bw[32];  // bias of the 64 columns as bf16 pairs (same for all lanes)
         if (args.bias != nullptr) {
           const uint4* bp = reinterpret_cast<const uint4*>(args.bias + c0);
@@ -266,6 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
               const float fa = pass == 0 ? cosf(a) : sinf(a);
               const float fb = pass == 0 ? cosf(b) : sinf(b);
               packed[i] = pack_bf16x2(fa * args.scale * tscale, fb * args.scale * tscale);
+            } else if (ident) {
+              packed[i] = pack_bf16x2(a, b);
             } else {
               packed[i] = pack_bf16x2(activate<ACT, true>(a) * tscale, activate<ACT, true>(b) * tscale);
             }
@@ -369,6 +375,10 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   a.K = (int)K;
   a.heads = (int)heads;
   a.nsets = nsets;
+  a.m = (int)(N / heads);
+  a.ident_from = (int)N;
+  a.tcol0 = 0;
+  a.tcol1 = (int)N;
   a.status = status;
   const int row_tiles = (int)((rows + BM - 1) / BM);
   const int total = row_tiles * (int)(N / BN) * nsets;
@@ -384,6 +394,44 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
     case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads) {
+  const int64_t N = 2 * feat + vdim;
+  return rows >= 1 && K >= BK && K % BK == 0 && N % BN == 0 && feat % 64 == 0 && heads >= 1 &&
+         feat % heads == 0 && (feat / heads) % 64 == 0 && rows <= (int64_t)INT32_MAX &&
+         K <= (int64_t)INT32_MAX / 2 && N <= (int64_t)INT32_MAX / 2;
+}
+
+cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, const void* temp,
+                             void* out, int64_t rows, int64_t K, int64_t feat, int64_t vdim,
+                             int64_t heads, cudaStream_t stream, int* status, bool* encoded) {
+  const int64_t N = 2 * feat + vdim;
+  CUtensorMap mA, mB, mC;
+  const bool ok = make_map_2d(&mA, x, (uint64_t)K, (uint64_t)rows, BK, BM) &&
+                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, BN) &&
+                  make_map_2d(&mC, out, (uint64_t)N, (uint64_t)rows, 64, 32);
+  *encoded = ok;
+  if (!ok) return cudaErrorInvalidValue;
+  PhiArgs a;
+  a.bias = (const __nv_bfloat16*)bias;
+  a.scale = 1.f;
+  a.temp0 = (const __nv_bfloat16*)temp;
+  a.temp1 = nullptr;
+  a.rows = (int)rows;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.heads = (int)heads;
+  a.nsets = 1;
+  a.m = (int)(feat / heads);
+  a.ident_from = (int)(2 * feat);  // [phi(q) | phi(k) * temp | v]
+  a.tcol0 = (int)feat;
+  a.tcol1 = (int)(2 * feat);
+  a.status = status;
+  const int row_tiles = (int)((rows + BM - 1) / BM);
+  const int total = row_tiles * (int)(N / BN);
+  const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
+  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, grid, stream);
 }
 
 }  // namespace fakla

@@ -864,11 +864,13 @@ __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const flo
 // Host side
 // ---------------------------------------------------------------------------
 static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
-                          int box_t = C) {
+                          int box_t = C, int64_t row_elems = 0) {
   // (B, T, H, 128) bf16 viewed as 4-D {d, h, t, b}; box = 64 d x 1 h x box_t t x 1 b.
+  // row_elems: elements from one token's row to the next (H * 128 when dense;
+  // larger for a column block of a wider row, e.g. the q/k/v GEMM output).
+  const int64_t re = row_elems > 0 ? row_elems : H * D;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2,
-                                 (cuuint64_t)T * H * D * 2};
+  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)re * 2, (cuuint64_t)T * re * 2};
   const cuuint32_t box[4] = {64, 1, (cuuint32_t)box_t, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
@@ -900,10 +902,12 @@ size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
 cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
-                              cudaStream_t stream, int* status, bool* encoded) {
+                              cudaStream_t stream, int* status, bool* encoded, int64_t in_row_elems) {
   CUtensorMap mQ, mK, mV, mO;
-  const bool ok = make_map_bthd(&mQ, q, B, T, H) && make_map_bthd(&mK, k, B, T, H) &&
-                  make_map_bthd(&mV, v, B, T, H) && make_map_bthd(&mO, out, B, T, H, 32);
+  const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems) &&
+                  make_map_bthd(&mK, k, B, T, H, C, in_row_elems) &&
+                  make_map_bthd(&mV, v, B, T, H, C, in_row_elems) &&
+                  make_map_bthd(&mO, out, B, T, H, 32);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   const int64_t nchunks = (T + C - 1) / C;

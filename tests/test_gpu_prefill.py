@@ -202,3 +202,59 @@ def test_prefill_host_rejects_device_inputs(cuda):
         fa_kla_host(x.to(cuda), x, torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), phi_weight=W.to(cuda))
     with pytest.raises(RuntimeError, match="CUDA"):
         fa_kla_host(x, x, torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), phi_weight=W)
+
+
+@pytest.mark.parametrize("T,with_temp", [(300, True), (1024, False)])
+def test_module_qkv_folded_into_phi(cuda, T, with_temp):
+    """Inference through fakla_qkv_prefill (projections folded into the feature
+    map, one GEMM for [phi(q) | phi(k) temp | v]): equal to the projections,
+    map and attention of the reference restated in float64 on the same bf16
+    parameters, within the bf16 bars; the returned state too."""
+    from pulsartecture_b200.attention import TMLinKernelAttn
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    torch.manual_seed(7)
+    E, H, D = 512, 4, 128
+    mapper = LearnablePositiveMap(H * D, H * D, dtype=torch.bfloat16)
+    mod = TMLinKernelAttn(E, mapper, num_heads=H, qk_dim=D, v_dim=D, temp_input_dim=16 if with_temp else 0,
+                          dtype=torch.bfloat16).to(cuda).eval()
+    x = (gen((2, T, E), 140) * 0.5).bfloat16().to(cuda)
+    ti = gen((2, T, 16), 141).bfloat16().to(cuda) if with_temp else None
+    with torch.no_grad():
+        assert mod._qkv_foldable(x)
+        y, (S, z) = mod(x, temp_input=ti, return_state=True)
+        temp = mod.temp_func(ti) if with_temp else None
+    sd = {k: to_np(v).astype(np.float64) for k, v in mod.state_dict().items()}
+    xd = to_np(x).astype(np.float64)
+
+    def lin(name):
+        return xd @ sd[f"{name}.linear.weight"].T + sd[f"{name}.linear.bias"]
+
+    eo, eS, ez = O.prefill(lin("proj_q"), lin("proj_k"), lin("proj_v").reshape(2, T, H, D),
+                           sd["feature_mapper.mlp.0.weight"], sd["feature_mapper.mlp.0.bias"],
+                           None if temp is None else to_np(temp))
+    got = to_np(y).reshape(2, T, H, D)
+    assert rel_l2(got, eo) < BF16_REL_L2
+    assert np.abs(got - eo).max() < BF16_MAX_ABS
+    assert rel_l2(to_np(S), eS) < BF16_REL_L2
+    assert rel_l2(to_np(z), ez) < BF16_REL_L2
+
+
+def test_module_qkv_fold_only_where_supported(cuda):
+    """The fold needs bf16, 128-wide heads and a 256-multiple GEMM width; other
+    modules keep the unfused path, and training keeps the autograd path."""
+    from pulsartecture_b200.attention import TMLinKernelAttn
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    x = torch.zeros(1, 8, 384, dtype=torch.bfloat16, device=cuda)
+    mod = TMLinKernelAttn(384, LearnablePositiveMap(384, 384, dtype=torch.bfloat16), num_heads=3, qk_dim=128,
+                          v_dim=128, dtype=torch.bfloat16).to(cuda).eval()
+    assert not mod._qkv_foldable(x)  # 3 heads: the [q|k|v] width 1152 is not a multiple of 256
+    with torch.no_grad():
+        assert mod(x).shape == (1, 8, 384)
+    mod4 = TMLinKernelAttn(512, LearnablePositiveMap(512, 512, dtype=torch.bfloat16), num_heads=4, qk_dim=128,
+                           v_dim=128, dtype=torch.bfloat16).to(cuda)
+    x4 = torch.zeros(1, 8, 512, dtype=torch.bfloat16, device=cuda)
+    assert not mod4._qkv_foldable(x4)  # grad enabled with trainable parameters
+    with torch.no_grad():
+        assert mod4._qkv_foldable(x4)
