@@ -33,9 +33,13 @@
 namespace fakla {
 namespace {
 
-constexpr int kThreads = 256;
+// 1024 threads with at most 16 state values each (per layout): short FMA
+// chains per token and 8 warps per scheduler to hide their latency; with 256
+// threads and 64 values the sweeps were latency-bound and the reverse one
+// spilled.
+constexpr int kThreads = 1024;
 constexpr int kTok = 16;
-constexpr int kMaxVals = 64;  // state values per thread per layout
+constexpr int kMaxVals = 16;  // state values per thread per layout
 
 struct BwdShape {
   int Df, Dv;
@@ -50,7 +54,7 @@ __host__ __device__ inline BwdShape bwd_shape(int Df, int Dv) {
   s.Df = Df;
   s.Dv = Dv;
   int J = 1;
-  while (Df * J * 2 <= kThreads) J *= 2;
+  while (Df * J * 2 <= kThreads && J < 32) J *= 2;
   s.J = J;
   s.nr = (Dv + J - 1) / J;
   s.Gc = kThreads / Dv;
