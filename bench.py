@@ -240,8 +240,8 @@ def run_only(args):
     """One kernel of the path alone, on the benchmark's shapes: `phi` = the
     phi GEMM for q and k of config 2 (2*65536 rows), `scan` = the chunk scan of
     config 2 on precomputed phi, `decode` = the decode state kernel of config 4,
-    `backward` = the attention backward (both sweeps) on config 2's mapped
-    shapes. Prints the mean device time per launch."""
+    `backward` = the attention backward (temperature included) on config 2's
+    mapped shapes. Prints the mean device time per launch."""
     from pulsartecture_b200 import _lib
 
     dev = torch.device("cuda", 0)
@@ -276,15 +276,17 @@ def run_only(args):
         km = (torch.rand(B, T, H, D, generator=g, device=dev) + 0.5).bfloat16()
         v = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
         do = (torch.randn(B, T, H, D, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+        tp = (torch.rand(B, T, H, generator=g, device=dev) + 0.5).bfloat16()
         dq, dk, dv = torch.empty_like(qm), torch.empty_like(km), torch.empty_like(v)
+        dtp = torch.empty_like(tp)
         wsb = L.fakla_attention_backward_workspace_bytes(B, T, H, D, D, _lib.FAKLA_BF16)
         ws = torch.empty(wsb, device=dev, dtype=torch.uint8)
 
         def bwd():
-            _lib.check(L.fakla_attention_backward(qm.data_ptr(), km.data_ptr(), v.data_ptr(), None, do.data_ptr(),
-                                                  None, None, None, None, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
-                                                  None, None, None, B, T, H, D, D, _lib.FAKLA_BF16, ws.data_ptr(), wsb,
-                                                  sh))
+            _lib.check(L.fakla_attention_backward(qm.data_ptr(), km.data_ptr(), v.data_ptr(), tp.data_ptr(),
+                                                  do.data_ptr(), None, None, None, None, dq.data_ptr(), dk.data_ptr(),
+                                                  dv.data_ptr(), dtp.data_ptr(), None, None, B, T, H, D, D,
+                                                  _lib.FAKLA_BF16, ws.data_ptr(), wsb, sh))
         fn = bwd
     else:
         S = torch.randn(DEC_N, DEC_H, D, D, generator=g, device=dev) * 0.02

@@ -309,11 +309,13 @@ extern "C" int fakla_phi(const void* x, const void* W, const void* bias, const v
 
 extern "C" size_t fakla_attention_backward_workspace_bytes(int64_t B, int64_t T, int64_t H,
                                                            int64_t Df, int64_t Dv, int dtype) {
-  (void)Df;
-  (void)Dv;
-  (void)dtype;
   if (B < 1 || T < 1 || H < 1) return 0;
-  return round_up(fakla::backward_workspace_bytes(B, T, H), 256);
+  size_t need = fakla::backward_workspace_bytes(B, T, H);
+  if (fakla::backward_sm100_supported(dtype, B, T, H, Df, Dv)) {
+    const size_t tc = fakla::backward_sm100_workspace_bytes(B, T, H, fakla_sm_count());
+    if (tc > need) need = tc;
+  }
+  return round_up(need, 256);
 }
 
 extern "C" int fakla_attention_backward(const void* q, const void* k, const void* v,
@@ -344,6 +346,21 @@ extern "C" int fakla_attention_backward(const void* q, const void* k, const void
     return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 4-byte aligned");
   DeviceInfo* d = nullptr;
   if ((rc = require_device(&d))) return rc;
+  // Tensor cores: bf16 128x128 heads, 16-byte aligned tensors (TMA bases and
+  // float4 state rows) and a workspace sized on this device.
+  if (fakla::backward_sm100_supported(dtype, B, T, H, Df, Dv) && aligned16(q) && aligned16(k) &&
+      aligned16(v) && aligned16(dout) && aligned16(dq) && aligned16(dk) && aligned16(dv) &&
+      aligned16(workspace) && (S0 == nullptr || aligned16(S0)) &&
+      (dS_final == nullptr || aligned16(dS_final)) && (dS0 == nullptr || aligned16(dS0)) &&
+      workspace_bytes >= fakla::backward_sm100_workspace_bytes(B, T, H, d->sms)) {
+    bool enc = false;
+    cudaError_t e = fakla::launch_backward_sm100(q, k, v, temp, dout, S0, z0, dS_final, dz_final,
+                                                 dq, dk, dv, dtemp, dS0, dz0, B, T, H, workspace,
+                                                 d->sms, (cudaStream_t)stream, d->status, &enc);
+    if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+    if (e != cudaSuccess) return cuda_fail(e, "attention backward (sm100) launch");
+    return FAKLA_OK;
+  }
   cudaError_t e = fakla::launch_backward_simt(dtype, q, k, v, temp, dout, S0, z0, dS_final,
                                               dz_final, dq, dk, dv, dtemp, dS0, dz0, B, T, H, Df,
                                               Dv, workspace, (cudaStream_t)stream);

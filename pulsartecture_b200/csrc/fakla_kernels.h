@@ -68,6 +68,45 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
                               cudaStream_t stream, int* status, bool* encoded,
                               int64_t in_row_elems = 0);
+
+// Tensor-core backward (sm100_backward.cu): bf16, Df = Dv = 128.
+bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
+size_t backward_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms);
+cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, const void* temp,
+                                  const void* dout, const float* S0, const float* z0,
+                                  const float* dS_final, const float* dz_final, void* dq, void* dk,
+                                  void* dv, void* dtemp, float* dS0, float* dz0, int64_t B,
+                                  int64_t T, int64_t H, void* workspace, int sms,
+                                  cudaStream_t stream, int* status, bool* encoded);
+// The backward scans (sm100_scan.cu, run by sm100_backward.cu). mode: 0 the
+// normalised forward (optionally writing den (B,T,H) and dden), 1 unnormalised causal with a per-row term `add` added to the kept q.k
+// products, 2 unnormalised reversed (suffix state; s >= t kept), 3 as 2 with
+// a per-column term. Epilogue of modes 1 and 3: out = (o + coef * vec[chunk]
+// + sigma_t mvec) * row_scale, coef = add[t] (mode 1) or 1 (mode 3), sigma_t =
+// the sum of row t's kept q'.k' + term over all chunks so far; dot_out[t] =
+// sum over d of the unscaled row times dot_rows[t]. state_in_T: S (with
+// FAKLA_STATE_IN) holds the initial state transposed. Modes 1-3 run one CTA
+// per sequence, without temp.
+struct ScanBackwardArgs {
+  int mode;
+  const float* add;
+  float* den_out;
+  int state_in_T;
+  const float* vec;
+  const float* mvec;  // modes 1, 3: v' was centred by this (B*H, D) vector
+  const void* row_scale;
+  const void* dot_rows;
+  void* dot_out;  // bf16
+  // mode 0: dden_out[t] = -(bf16(grad_rows[t] / den_t) . out_t); skip_out: no output rows
+  const void* grad_rows;
+  float* dden_out;
+  int skip_out;
+};
+cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, const void* temp,
+                                   void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                                   unsigned flags, const ScanBackwardArgs& m, void* workspace,
+                                   size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
+                                   bool* encoded);
 // q/k/v GEMM: out (rows, 2*feat + vdim) = [phi(q) | phi(k) * temp | v] from
 // x (rows, K) and W (2*feat + vdim, K).
 bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads);

@@ -1,0 +1,329 @@
+// FA-KLA backward on tensor cores (bf16, Df = Dv = 128): the gradients of
+// the recurrence of cpu_kernels.cpp:107-164 (simt_backward.cu states them)
+// as four chunked scans of sm100_scan.cu plus small fp32 passes.
+//
+// With dnum_t = dout_t / den_t, dden_t = -(dout_t . out_t) / den_t, k~ = k temp,
+// zb_c = z_0 + sum of k~ over the tokens before chunk c and
+// W_c = dz_T + sum of dden_t q_t over the tokens after chunk c:
+//
+//   1. sums of k~ per chunk  -> zb (prefix), m_k = mean of k~
+//   2. forward scan (mode 0) -> den_t, and dden_t from its fp32 output
+//   3. sums of dden q and q per chunk -> W (suffix), dz_0, m_q = mean of q
+//   4. prep                  dnum, k~, k~ - m_k, q - m_q (bf16)
+//   5. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m_k) with dden_t
+//            added to row t of q'k'^T, initial state S_0^T;
+//            epilogue + dden_t zb_c + sigma_t m_k
+//   6. dk~ = reversed scan of (q' = v, k' = dnum, v' = q - m_q) with dden_t
+//            added to column t, initial state dS_T^T;
+//            epilogue + W_c + sigma_s m_q, times temp_s -> dk; dtemp_s = dk~_s . k_s
+//   7. dv  = reversed scan of (q' = k~, k' = q, v' = dnum), initial state
+//            dS_T; its final state is dS_0
+// sigma_t is the sum of row t of (q'k'^T + term) over every key so far; the
+// scans form it from the chunk's row sum and q'.z' (z' = sum of k' rows).
+//
+// Precision: for positive feature maps the products behind dq and dk~ cancel
+// along the features' common direction (sum_s c_ts k~_s with sum_s w_s c_ts
+// = 0). The cancelling parts are therefore kept out of bf16: dden is formed
+// from the same bf16 dnum the scans multiply with (dden_t = -bf16(dnum_t) .
+// out_t, out_t in fp32), v' is centred so that only the small deviations
+// k~ - m_k (q - m_q) are rounded while the common part m enters in fp32 through
+// sigma and the exact zb / W, and the unnormalised scans carry their state as
+// bf16 hi + lo.
+//
+// Every intermediate is (B, T, H, .) like the inputs, so the scans take
+// them through the same tensor maps as the forward.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fakla.h"
+#include "fakla_common.cuh"
+#include "fakla_kernels.h"
+
+namespace fakla {
+namespace {
+
+constexpr int D = 128;
+constexpr int C = 128;  // scan chunk (tokens)
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// One (b, t, h) row per 16 threads (8 values each): dnum = bf16(dout / den)
+// (rounded as the forward scan's dden epilogue rounds it), k~ = k temp (when
+// kt is given), kc = k~ - m_k, qc = q - m_q (m per sequence (b, h)).
+__global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
+                                const float* __restrict__ den, const __nv_bfloat16* __restrict__ q,
+                                const __nv_bfloat16* __restrict__ k,
+                                const __nv_bfloat16* __restrict__ temp,
+                                const float* __restrict__ mk, const float* __restrict__ mq,
+                                __nv_bfloat16* __restrict__ dnum, __nv_bfloat16* __restrict__ kt,
+                                __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ qc,
+                                int64_t rows, int T, int H) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = gid >> 4;
+  const int part = (int)(gid & 15);
+  if (row >= rows) return;
+  const int64_t b = row / ((int64_t)T * H);
+  const int64_t bh = b * H + row % H;
+  const int64_t off = row * D + part * 8;
+  float g[8];
+  load8(dout + off, g);
+  const float inv = 1.f / den[row];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) g[e] *= inv;
+  store8(dnum + off, g);
+  const float tv = temp != nullptr ? __bfloat162float(temp[row]) : 1.f;
+  float kv[8], m[8];
+  load8(k + off, kv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) kv[e] *= tv;
+  if (kt != nullptr) store8(kt + off, kv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m[e] = mk[bh * D + part * 8 + e];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) kv[e] -= m[e];
+  store8(kc + off, kv);
+  float qv[8];
+  load8(q + off, qv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) qv[e] -= mq[bh * D + part * 8 + e];
+  store8(qc + off, qv);
+}
+
+// Per chunk c of sequence bh, 128 threads (one per feature f):
+//   s1[bh][c][f] = sum over the chunk's tokens t of w1_t x_t[f]   (w1 = 1 if null)
+//   s2[bh][c][f] = sum of x_t[f]                                  (if s2 given)
+// Grid (nchunks, B*H).
+__global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
+                                      const float* __restrict__ w1f,
+                                      const __nv_bfloat16* __restrict__ w1h,
+                                      float* __restrict__ s1, float* __restrict__ s2, int T, int H) {
+  const int c = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int f = threadIdx.x;
+  const int t0 = c * C;
+  const int t1 = min(T, t0 + C);
+  float a0 = 0.f, a1 = 0.f, u0 = 0.f, u1 = 0.f;
+  auto w1 = [&](int64_t r) {
+    return w1f != nullptr ? w1f[r] : (w1h != nullptr ? __bfloat162float(w1h[r]) : 1.f);
+  };
+  int t = t0;
+  for (; t + 1 < t1; t += 2) {
+    const int64_t r0 = ((int64_t)b * T + t) * H + h;
+    const int64_t r1 = r0 + H;
+    const float x0 = __bfloat162float(x[r0 * D + f]), x1 = __bfloat162float(x[r1 * D + f]);
+    a0 = fmaf(w1(r0), x0, a0);
+    a1 = fmaf(w1(r1), x1, a1);
+    u0 += x0;
+    u1 += x1;
+  }
+  if (t < t1) {
+    const int64_t r0 = ((int64_t)b * T + t) * H + h;
+    const float x0 = __bfloat162float(x[r0 * D + f]);
+    a0 = fmaf(w1(r0), x0, a0);
+    u0 += x0;
+  }
+  const int64_t o = ((int64_t)bh * gridDim.x + c) * D + f;
+  s1[o] = a0 + a1;
+  if (s2 != nullptr) s2[o] = u0 + u1;
+}
+
+// Exclusive prefix over the chunks (in place): s[c] <- init + sum_{c' < c} s[c'],
+// or with `reverse` the suffix init + sum_{c' > c} s[c']. total <- init + the
+// sum of all chunks, mean <- that sum / T (each if given). Grid B*H, 128 threads.
+__global__ void bwd_scan_chunks_kernel(float* __restrict__ s, const float* __restrict__ init,
+                                       float* __restrict__ total, float* __restrict__ mean,
+                                       int nchunks, int T, int reverse) {
+  const int64_t bh = blockIdx.x;
+  const int f = threadIdx.x;
+  const float base_val = init != nullptr ? init[bh * D + f] : 0.f;
+  float all = 0.f;
+  float* base = s + bh * nchunks * D + f;
+  for (int i = 0; i < nchunks; ++i) {
+    const int c = reverse ? nchunks - 1 - i : i;
+    const float v = base[(int64_t)c * D];
+    base[(int64_t)c * D] = base_val + all;
+    all += v;
+  }
+  if (total != nullptr) total[bh * D + f] = base_val + all;
+  if (mean != nullptr) mean[bh * D + f] = all / (float)T;
+}
+
+struct BwdLayout {
+  size_t den, zb, dnum, dden, kt, kc, qc, wq, sq, mk, mq, scan, total;
+};
+
+BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t rows = (size_t)(B * T * H);
+  const size_t nch = (size_t)((T + C - 1) / C);
+  const size_t chunk_vecs = up((size_t)(B * H) * nch * D * 4);
+  BwdLayout l;
+  size_t o = 0;
+  l.den = o;  o += up(rows * 4);
+  l.dden = o; o += up(rows * 4);
+  l.dnum = o; o += up(rows * D * 2);
+  l.kt = o;   o += temp ? up(rows * D * 2) : 0;
+  l.kc = o;   o += up(rows * D * 2);
+  l.qc = o;   o += up(rows * D * 2);
+  l.zb = o;   o += chunk_vecs;
+  l.wq = o;   o += chunk_vecs;
+  l.sq = o;   o += chunk_vecs;
+  l.mk = o;   o += up((size_t)(B * H) * D * 4);
+  l.mq = o;   o += up((size_t)(B * H) * D * 4);
+  l.scan = o; o += up(scan_sm100_workspace_bytes(B, T, H, sms));
+  l.total = o;
+  return l;
+}
+
+}  // namespace
+
+bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+  return dtype == FAKLA_BF16 && scan_sm100_supported(B, T, H, Df, Dv) &&
+         B * T * H <= (int64_t)INT32_MAX;
+}
+
+size_t backward_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
+  // sized for the temp case (the k~ buffer); without temp it goes unused
+  return bwd_layout(B, T, H, true, sms).total;
+}
+
+cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, const void* temp,
+                                  const void* dout, const float* S0, const float* z0,
+                                  const float* dS_final, const float* dz_final, void* dq, void* dk,
+                                  void* dv, void* dtemp, float* dS0, float* dz0, int64_t B,
+                                  int64_t T, int64_t H, void* workspace, int sms,
+                                  cudaStream_t stream, int* status, bool* encoded) {
+  const BwdLayout l = bwd_layout(B, T, H, temp != nullptr, sms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto* den = reinterpret_cast<float*>(ws + l.den);
+  auto* dden = reinterpret_cast<float*>(ws + l.dden);
+  auto* dnum = reinterpret_cast<__nv_bfloat16*>(ws + l.dnum);
+  auto* kt = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kt) : nullptr;
+  auto* kc = reinterpret_cast<__nv_bfloat16*>(ws + l.kc);
+  auto* qc = reinterpret_cast<__nv_bfloat16*>(ws + l.qc);
+  auto* zb = reinterpret_cast<float*>(ws + l.zb);
+  auto* wq = reinterpret_cast<float*>(ws + l.wq);
+  auto* sq = reinterpret_cast<float*>(ws + l.sq);
+  auto* mk = reinterpret_cast<float*>(ws + l.mk);
+  auto* mq = reinterpret_cast<float*>(ws + l.mq);
+  void* scan_ws = ws + l.scan;
+  const size_t scan_bytes = l.total - l.scan;
+  const int64_t rows = B * T * H;
+  const int nch = (int)((T + C - 1) / C);
+  const dim3 cgrid((unsigned)nch, (unsigned)(B * H));
+  const auto* qh = static_cast<const __nv_bfloat16*>(q);
+  const auto* kh = static_cast<const __nv_bfloat16*>(k);
+  const auto* th = static_cast<const __nv_bfloat16*>(temp);
+  cudaError_t e;
+
+  // 1. zb (z before each chunk, from z_0) and m_k: sums of k~ per chunk
+  bwd_chunk_sums_kernel<<<cgrid, D, 0, stream>>>(kh, nullptr, th, zb, nullptr, (int)T, (int)H);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(zb, z0, nullptr, mk, nch, (int)T, 0);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  // 2. forward: den and dden (no output rows: dq only names a valid tensor
+  // for the output map)
+  ScanBackwardArgs m{};
+  m.mode = 0;
+  m.den_out = den;
+  m.grad_rows = dout;
+  m.dden_out = dden;
+  m.skip_out = 1;
+  const unsigned in0 = S0 != nullptr ? FAKLA_STATE_IN : 0u;
+  e = launch_scan_sm100_mode(q, k, v, temp, dq, const_cast<float*>(S0), const_cast<float*>(z0), B,
+                             T, H, in0, m, scan_ws, scan_bytes, sms, stream, status, encoded);
+  if (e != cudaSuccess) return e;
+
+  // 3. W (suffix sums of dden q from dz_T), dz_0, m_q
+  bwd_chunk_sums_kernel<<<cgrid, D, 0, stream>>>(qh, dden, nullptr, wq, sq, (int)T, (int)H);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(wq, dz_final, dz0, nullptr, nch,
+                                                              (int)T, 1);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(sq, nullptr, nullptr, mq, nch,
+                                                              (int)T, 0);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+
+  // 4. dnum, k~, k~ - m_k, q - m_q
+  {
+    const int64_t threads = rows * 16;
+    bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+        (const __nv_bfloat16*)dout, den, qh, kh, th, mk, mq, dnum, kt, kc, qc, rows, (int)T, (int)H);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const void* ktil = temp != nullptr ? (const void*)kt : k;
+
+  // 5. dq
+  m = ScanBackwardArgs{};
+  m.mode = 1;
+  m.add = dden;
+  m.vec = zb;
+  m.mvec = mk;
+  m.state_in_T = 1;
+  e = launch_scan_sm100_mode(dnum, v, kc, nullptr, dq, const_cast<float*>(S0), nullptr, B, T, H,
+                             in0, m, nullptr, 0, sms, stream, status, encoded);
+  if (e != cudaSuccess) return e;
+
+  // 6. dk (and dtemp); before dv, whose final state may overwrite dS_T in place
+  m = ScanBackwardArgs{};
+  m.mode = 3;
+  m.add = dden;
+  m.vec = wq;
+  m.mvec = mq;
+  m.state_in_T = 1;
+  m.row_scale = temp;
+  if (temp != nullptr && dtemp != nullptr) {
+    m.dot_rows = k;
+    m.dot_out = dtemp;
+  }
+  const unsigned fk = dS_final != nullptr ? FAKLA_STATE_IN : 0u;
+  e = launch_scan_sm100_mode(v, dnum, qc, nullptr, dk, const_cast<float*>(dS_final), nullptr, B, T,
+                             H, fk, m, nullptr, 0, sms, stream, status, encoded);
+  if (e != cudaSuccess) return e;
+
+  // 7. dv (and dS_0 as the reversed scan's final state)
+  float* Sv = nullptr;
+  unsigned fv = 0;
+  if (dS0 != nullptr) {
+    Sv = dS0;
+    fv |= FAKLA_STATE_OUT;
+    if (dS_final != nullptr) {
+      if (dS_final != dS0 &&
+          (e = cudaMemcpyAsync(dS0, dS_final, (size_t)(B * H) * D * D * sizeof(float),
+                               cudaMemcpyDeviceToDevice, stream)) != cudaSuccess)
+        return e;
+      fv |= FAKLA_STATE_IN;
+    }
+  } else if (dS_final != nullptr) {
+    Sv = const_cast<float*>(dS_final);
+    fv |= FAKLA_STATE_IN;
+  }
+  m = ScanBackwardArgs{};
+  m.mode = 2;
+  return launch_scan_sm100_mode(ktil, q, dnum, nullptr, dv, Sv, nullptr, B, T, H, fv, m, nullptr, 0,
+                                sms, stream, status, encoded);
+}
+
+}  // namespace fakla

@@ -81,6 +81,9 @@ constexpr size_t kOffM0 = kOffV + kStages * kTile;
 constexpr size_t kOffM1 = kOffM0 + 1024;
 constexpr size_t kOffSb = kOffM1 + 1024;
 constexpr size_t kOperandBytes = kOffSb + kTile;
+// The unnormalised modes keep one K tile (stage 0) and use the second K slot
+// for Sb_lo: their state enters MMA2 as bf16 hi + lo (the backward's
+// products cancel to small results, where one bf16 rounding of S shows).
 constexpr size_t kHeadBytes = 256;
 constexpr size_t kSmemBytes = 1024 + kOperandBytes;  // 232448 = the sm_100 per-CTA maximum
 constexpr uint32_t kSmallSbo = 2048;                 // rows 8-15 of the N=16 operands
@@ -97,6 +100,7 @@ enum Bar {
   kOFree,
   kKReady,
   kDrain,
+  kKFree,   // unnormalised modes: the single K tile read by MMA4
   kNumBars
 };
 static_assert(kNumBars * 8 + 8 <= kHeadBytes, "barrier area");
@@ -111,7 +115,33 @@ struct ScanArgs {
   int seg_chunks;             // chunks per segment
   unsigned flags;
   int* status;
+  // backward passes (modes below)
+  const __nv_bfloat16* grad_rows;  // kScanNormal: (B,T,H,D) output gradient -> dden_out, or null
+  float* dden_out;                 // (B,T,H): -(bf16(g/den) . out) (g = grad_rows)
+  int skip_out;                    // do not store the output rows
+  const float* add;           // (B,T,H) per-token term added to the kept P entries, or null
+  float* den_out;             // (B,T,H) denominators of the normalised mode, or null
+  int state_in_T;             // the initial state is given transposed (S[dv][f])
+  // backward epilogues: out = (o + coef * vec[chunk] + sigma_t mvec) * row_scale,
+  // coef = add[t] in kScanRowAdd and 1 in kScanRevCol, sigma_t = the row's
+  // kept q'.k' + term summed over all chunks so far (the centring term of
+  // v' = v - mvec); dot_out[t] = sum(that unscaled row * dot_rows[t])
+  const float* vec;           // (B*H, nchunks, D), or null
+  const float* mvec;          // (B*H, D), or null
+  const __nv_bfloat16* row_scale;  // (B,T,H), or null
+  const __nv_bfloat16* dot_rows;   // (B,T,H,D) with dot_out, or null
+  __nv_bfloat16* dot_out;          // (B,T,H), or null
 };
+
+// Modes of scan_sm100_kernel. The backward of FA-KLA is three unnormalised
+// scans of the same shape as the forward one (simt_backward.cu gives the
+// formulas; sm100_backward.cu runs them):
+//   kScanNormal  out = (q S_{<c} + (M o Q K^T) V) / den        (the forward)
+//   kScanRowAdd  out = q S_{<c} + (M o (Q K^T + a 1^T)) V       (dq: a = dden)
+//   kScanRevRaw  out = q S_{>c} + (M' o Q K^T) V                (dv, reversed time)
+//   kScanRevCol  out = q S_{>c} + (M' o (Q K^T + 1 b^T)) V      (dk~, reversed: b = dden)
+// M keeps s <= t; M' keeps s >= t and the chunks are walked from the end.
+enum { kScanNormal = 0, kScanRowAdd = 1, kScanRevRaw = 2, kScanRevCol = 3 };
 
 __device__ __forceinline__ uint64_t kdesc(uint32_t tile_addr, int j) {
   // K-major operand, K step j (16 elements): atom j/4, +32 B per step inside.
@@ -161,6 +191,11 @@ __device__ __forceinline__ float temp_at(const __nv_bfloat16* temp, int b, int T
   return t < T ? __bfloat162float(temp[((int64_t)b * T + t) * H + h]) : 0.f;
 }
 
+// Per-token fp32 term of the backward scans (0 past the end of the sequence).
+__device__ __forceinline__ float add_at(const float* add, int b, int T, int H, int h, int t) {
+  return t < T ? add[((int64_t)b * T + t) * H + h] : 0.f;
+}
+
 // Write z_f as bf16 hi (row 0) and lo (row 1) of the ZK operand.
 __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
   const __nv_bfloat16 hi = __float2bfloat16_rn(zf);
@@ -172,20 +207,29 @@ __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
 
 // Tokens [sbase, sbase+32) of row r of P (fp32 bits in v), split into bf16
 // hi + lo and stored in place: hi in columns sbase + [0,16), lo in sbase +
-// [16,32) (two tokens per column). kMask keeps only s <= r (the 32-token group
-// on the diagonal); groups below it are kept whole. Returns the sum of the
-// kept values.
-template <bool kMask>
+// [16,32) (two tokens per column). kMask: 0 keeps the whole group, 1 keeps
+// s <= r (causal diagonal group), 2 keeps s >= r (reversed diagonal group).
+// The kept values first get `arow` (a per-row term) and bcol[s - sbase] (a
+// per-column term, held by lane s - sbase of the warp). Returns the sum of
+// the kept values.
+template <int kMask, bool kCol>
 __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase, int r,
-                                             uint32_t p_addr) {
+                                             uint32_t p_addr, float arow, float bcol) {
   uint32_t hi[16], lo[16];
   float rs = 0.f;
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    float x0 = __uint_as_float(v[2 * e]), x1 = __uint_as_float(v[2 * e + 1]);
-    if (kMask) {
+    float x0 = __uint_as_float(v[2 * e]) + arow, x1 = __uint_as_float(v[2 * e + 1]) + arow;
+    if (kCol) {
+      x0 += __shfl_sync(0xffffffffu, bcol, 2 * e);
+      x1 += __shfl_sync(0xffffffffu, bcol, 2 * e + 1);
+    }
+    if (kMask == 1) {
       x0 = sbase + 2 * e <= r ? x0 : 0.f;
       x1 = sbase + 2 * e + 1 <= r ? x1 : 0.f;
+    } else if (kMask == 2) {
+      x0 = sbase + 2 * e >= r ? x0 : 0.f;
+      x1 = sbase + 2 * e + 1 >= r ? x1 : 0.f;
     }
     rs += x0 + x1;
     const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
@@ -200,19 +244,42 @@ __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase,
 }
 
 // Row r of P, token group g (32 tokens) of a warp whose rows are the group
-// q4: below the diagonal (g < q4) kept whole, on it (g == q4) masked.
+// q4. Causal: groups below the diagonal are kept whole, the diagonal one is
+// masked. Reversed: groups above the diagonal are kept whole.
+template <bool kRev, bool kCol>
 __device__ __forceinline__ float split_group_at(const uint32_t (&v)[32], int g, int q4, int r,
-                                                uint32_t p_addr) {
-  return g == q4 ? split_group<true>(v, 32 * g, r, p_addr) : split_group<false>(v, 32 * g, r, p_addr);
+                                                uint32_t p_addr, float arow, float bcol) {
+  return g == q4 ? split_group<kRev ? 2 : 1, kCol>(v, 32 * g, r, p_addr, arow, bcol)
+                 : split_group<0, kCol>(v, 32 * g, r, p_addr, arow, bcol);
 }
 
-// Above the diagonal the whole group is masked: hi = lo = 0.
+// Outside the kept triangle the whole group is masked: hi = lo = 0.
 __device__ __forceinline__ void zero_group(int g, uint32_t p_addr) {
   uint32_t zz[16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) zz[e] = 0u;
   tmem_st16(p_addr + (uint32_t)(32 * g), zz);
   tmem_st16(p_addr + (uint32_t)(32 * g + 16), zz);
+}
+
+// State row r, columns [c, c+8) into the MN-major bf16 operand Sb (and, with
+// kLo, the residual S - bf16(S) into Sb_lo).
+template <bool kLo>
+__device__ __forceinline__ void put_sb8(uint8_t* sb, uint8_t* sb_lo, int r, int c, const float* f) {
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+    if (kLo) {
+      const float2 hf = __bfloat1622float2(h2);
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(f[2 * e] - hf.x, f[2 * e + 1] - hf.y);
+      lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
+    }
+  }
+  const uint32_t off = (c >= 64 ? kAtom : 0) + sw128_offset((uint32_t)r, (uint32_t)(c & 63));
+  *reinterpret_cast<uint4*>(sb + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  if (kLo) *reinterpret_cast<uint4*>(sb_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 // 32 fp32 values (bits in v) times inv, written as bf16 into row r, columns
@@ -231,6 +298,72 @@ __device__ __forceinline__ void stage_scaled_32(const uint32_t (&v)[32], float i
   }
 }
 
+// sum over columns [c, c+32) of bf16(g * inv) * (x * inv): x = out * den
+// (fp32 bits in v), g = the output gradient row (bf16, global memory).
+__device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, const __nv_bfloat16* g) {
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float gf[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(g + 8 * k), gf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float dn = __bfloat162float(__float2bfloat16_rn(gf[e] * inv));
+      acc = fmaf(dn, __uint_as_float(v[8 * k + e]) * inv, acc);
+    }
+  }
+  return acc;
+}
+
+__device__ __forceinline__ void load_f32x8(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+// Backward epilogue of one row: y = (x + coef * vec + sig * mv) * scale over
+// columns [col0, col0+32) (vec, mv: fp32 in global memory, the same for
+// every row of the chunk; mv may be null), written as bf16 like
+// stage_scaled_32. With kDot the return value is sum(x + coef * vec + sig *
+// mv) * drow over these columns (drow: bf16 row in global memory), else 0.
+template <bool kDot>
+__device__ __forceinline__ float stage_affine_32(const uint32_t (&v)[32], float coef, const float* vec,
+                                                 float sig, const float* mv, float scale,
+                                                 const __nv_bfloat16* drow, uint8_t* tile, int r,
+                                                 int col0) {
+  uint8_t* atom = tile + (col0 >= 64 ? kAtom : 0);
+  float dot = 0.f;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float wv[8], mvv[8];
+    load_f32x8(vec + col0 + 8 * g, wv);
+    if (mv != nullptr) {
+      load_f32x8(mv + col0 + 8 * g, mvv);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mvv[e] = 0.f;
+    }
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      y[e] = fmaf(sig, mvv[e], fmaf(coef, wv[e], __uint_as_float(v[8 * g + e])));
+    if (kDot) {
+      float kf[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(drow + col0 + 8 * g), kf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot = fmaf(y[e], kf[e], dot);
+    }
+    uint4 u;
+    u.x = pack_bf16x2(y[0] * scale, y[1] * scale);
+    u.y = pack_bf16x2(y[2] * scale, y[3] * scale);
+    u.z = pack_bf16x2(y[4] * scale, y[5] * scale);
+    u.w = pack_bf16x2(y[6] * scale, y[7] * scale);
+    *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((col0 & 63) + 8 * g))) = u;
+  }
+  return dot;
+}
+
 // Warp-uniform forms of the bounded wait and of the abort check, for warps
 // that go on to issue .sync.aligned tcgen05 loads and stores.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
@@ -245,6 +378,7 @@ __device__ __forceinline__ uint8_t* operand_base(uint8_t* raw) {
                                     ~uintptr_t(1023));
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -265,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   uint8_t* sV = smem + kOffV;
   uint8_t* sM0 = smem + kOffM0;
   uint8_t* sSb = smem + kOffSb;
+  uint8_t* sSbLo = smem + kOffK + kTile;  // unnormalised modes only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -278,6 +413,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   const int nch = c1 - c0;
   const bool has_temp = args.temp != nullptr;
   const bool last_seg = seg == args.G - 1;
+  constexpr bool kRaw = MODE != kScanNormal;     // no normaliser: q.z, z and den are not formed
+  constexpr bool kRev = MODE >= kScanRevRaw;     // chunks from the end, s >= t kept
+  // the k' row sum z (MMA4b) and q'.z (MMA2b): the normaliser of mode 0, the
+  // centring terms of modes 1 and 3
+  constexpr bool kZ = MODE != kScanRevRaw;
+  auto k_tile = [&](int st) { return sK + (kRaw ? 0 : st * kTile); };
+  // first token of this CTA's chunk i
+  auto chunk_t0 = [&](int i) {
+    const int ci = c0 + i;
+    return (kRev ? nchunks_total - 1 - ci : ci) * C;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -293,6 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     mbar_init(&bars[kOFree], 4);
     mbar_init(&bars[kKReady], 4);
     mbar_init(&bars[kDrain], 1);
+    mbar_init(&bars[kKFree], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -327,12 +474,24 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         }
         uint64_t* fb = &bars[kFull0 + st];
         mbar_arrive_expect_tx(fb, 3 * kTile);
-        const int t0 = (c0 + i) * C;
-        for (int a = 0; a < 2; ++a) {
-          tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
-          tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
+        const int t0 = chunk_t0(i);
+        if constexpr (kRaw) {
+          for (int a = 0; a < 2; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
+          ++issued;
+          // one K tile: MMA4 of the previous chunk must have read it
+          if (i > 0 && !mbar_wait(&bars[kKFree], (uint32_t)(i - 1) & 1u, kWaitNs)) {
+            report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          for (int a = 0; a < 2; ++a) tma_load_4d(sK + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+        } else {
+          for (int a = 0; a < 2; ++a) {
+            tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+            tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
+          }
+          ++issued;
         }
-        ++issued;
         // The Q tile doubles as the output staging of chunk i-2: wait for
         // that store to have read it.
         if (!mbar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
@@ -359,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       constexpr uint32_t idKV = idesc_bf16_f32(128, 128, true, true);    // K^T . V
       constexpr uint32_t idK1 = idesc_bf16_f32(128, 16, true, false);    // K^T . 1
       const uint32_t aSb = smem_u32(sSb);
+      const uint32_t aSbLo = smem_u32(sSbLo);
       const uint32_t aM0 = smem_u32(sM0);
       bool ok = true;
       bool issued_any = false;
@@ -371,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (!ok) break;
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + st * kTile);
-        const uint32_t aK = smem_u32(sK + st * kTile);
+        const uint32_t aK = smem_u32(k_tile(st));
         const uint32_t aV = smem_u32(sV + st * kTile);
         issued_any = true;
         // MMA1: P = Q K^T (overwrites the hi/lo of the previous chunk, which
@@ -386,13 +546,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         // MMA2 / MMA2b: O = Q S_{<c}, Dz = Q [z_hi z_lo]
 #pragma unroll
         for (int j = 0; j < 8; ++j) mma_ss(tmem + kColO, kdesc(aQ, j), mndesc(aSb, j), idQS, j > 0);
+        if constexpr (kRaw) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColDz, kdesc(aQ, j), zkdesc(aM0, j), idQZ, j > 0);
+          for (int j = 0; j < 8; ++j) mma_ss(tmem + kColO, kdesc(aQ, j), mndesc(aSbLo, j), idQS, 1u);
+        }
+        if constexpr (kZ) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) mma_ss(tmem + kColDz, kdesc(aQ, j), zkdesc(aM0, j), idQZ, j > 0);
+        }
         // MMA4 / MMA4b: S += K^T V, z += K^T 1 (A = K as M=f x K=s, MN-major)
 #pragma unroll
         for (int j = 0; j < 8; ++j) mma_ss(tmem + kColS, mndesc(aK, j), mndesc(aV, j), idKV, 1u);
+        if constexpr (kZ) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mma_ss(tmem + kColZ, mndesc(aK, j), onesdesc(aM0, j), idK1, 1u);
+          for (int j = 0; j < 8; ++j) mma_ss(tmem + kColZ, mndesc(aK, j), onesdesc(aM0, j), idK1, 1u);
+        }
+        // the last reader of the single K tile of the unnormalised modes
+        if constexpr (kRaw) mma_commit(&bars[kKFree]);
         mma_commit(&bars[kBarS]);
         ok = mbar_wait(&bars[kE1Done], par, kWaitNs);
         if (!ok) break;
@@ -430,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         const int st = i & 1;
         ok = warp_wait(&bars[kFull0 + st], (uint32_t)(i >> 1) & 1u);
         if (!ok) break;
-        scale_k_row(sK + st * kTile, r, temp_at(args.temp, b, args.T, args.H, h, (c0 + i) * C + r));
+        scale_k_row(sK + st * kTile, r, temp_at(args.temp, b, args.T, args.H, h, chunk_t0(i) + r));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kKReady]);
@@ -439,23 +609,35 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       if (!ok) break;
       tc_fence_after();
       // Token groups of 32: this warp's rows are group q4, so group g is
-      // whole (g < q4), diagonal (g == q4) or empty (g > q4) for every lane.
+      // whole, diagonal or empty for every lane (causal: whole below the
+      // diagonal; reversed: whole above it).
       const uint32_t p_addr = lane_addr + kColP;
+      const int t0 = chunk_t0(i);
+      constexpr bool kCol = MODE == kScanRevCol;
+      const float arow = MODE == kScanRowAdd ? add_at(args.add, b, args.T, args.H, h, t0 + r) : 0.f;
       float rs = 0.f;
 #pragma unroll 1
       for (int g0 = 0; g0 < 4; g0 += 2) {
-        if (g0 > q4) {
+        const bool k0 = kRev ? g0 >= q4 : g0 <= q4;
+        const bool k1 = kRev ? g0 + 1 >= q4 : g0 + 1 <= q4;
+        if (!k0 && !k1) {
           zero_group(g0, p_addr);
           zero_group(g0 + 1, p_addr);
           continue;
         }
         uint32_t va[32], vb[32];
-        tmem_ld32(p_addr + (uint32_t)(32 * g0), va);
-        if (g0 + 1 <= q4) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
+        if (k0) tmem_ld32(p_addr + (uint32_t)(32 * g0), va);
+        if (k1) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
         tmem_ld_wait();
-        rs += split_group_at(va, g0, q4, r, p_addr);
-        if (g0 + 1 <= q4)
-          rs += split_group_at(vb, g0 + 1, q4, r, p_addr);
+        // per-column terms of tokens 32g + lane (broadcast inside split_group)
+        const float b0 = kCol ? add_at(args.add, b, args.T, args.H, h, t0 + 32 * g0 + lane) : 0.f;
+        const float b1 = kCol ? add_at(args.add, b, args.T, args.H, h, t0 + 32 * g0 + 32 + lane) : 0.f;
+        if (k0)
+          rs += split_group_at<kRev, kCol>(va, g0, q4, r, p_addr, arow, b0);
+        else
+          zero_group(g0, p_addr);
+        if (k1)
+          rs += split_group_at<kRev, kCol>(vb, g0 + 1, q4, r, p_addr, arow, b1);
         else
           zero_group(g0 + 1, p_addr);
       }
@@ -476,16 +658,21 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     const int64_t bh = (int64_t)b * args.H + h;
     {
-      // initial state: the segment's record, else the caller's state, else 0
+      // initial state: the segment's record, else the caller's state (by rows,
+      // or transposed: column r), else 0
       const float* srow = nullptr;
+      const float* scol = nullptr;
       float z0 = 0.f;
       if (args.seg_init != nullptr) {
         const float* rec = args.seg_init + (bh * args.G + seg) * kStateFloats;
         srow = rec + (int64_t)r * D;
         z0 = rec[(int64_t)D * D + r];
       } else if ((args.flags & FAKLA_STATE_IN) && args.S != nullptr) {
-        srow = args.S + (bh * D + r) * D;
-        z0 = args.z[bh * D + r];
+        if (args.state_in_T)
+          scol = args.S + bh * D * D + r;
+        else
+          srow = args.S + (bh * D + r) * D;
+        if (!kRaw) z0 = args.z[bh * D + r];
       }
 #pragma unroll 1
       for (int cc = 0; cc < D; cc += 16) {
@@ -501,6 +688,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
             f[4 * g + 2] = x.z;
             f[4 * g + 3] = x.w;
           }
+        } else if (scol != nullptr) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = scol[(int64_t)(cc + e) * D];
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) f[e] = 0.f;
@@ -508,16 +698,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
 #pragma unroll
         for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(f[e]);
         tmem_st16(lane_addr + kColS + (uint32_t)cc, v);
-        uint32_t p[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(f[2 * e], f[2 * e + 1]);
-        uint8_t* atom = sSb + (cc >= 64 ? kAtom : 0);
-        const int col = cc & 63;
-        *reinterpret_cast<uint4*>(atom + sw128_offset(r, col)) = make_uint4(p[0], p[1], p[2], p[3]);
-        *reinterpret_cast<uint4*>(atom + sw128_offset(r, col + 8)) = make_uint4(p[4], p[5], p[6], p[7]);
+        put_sb8<kRaw>(sSb, sSbLo, r, cc, f);
+        put_sb8<kRaw>(sSb, sSbLo, r, cc + 8, f + 8);
       }
-      tmem_st1(lane_addr + kColZ, __float_as_uint(z0));
-      put_zk(sM0, r, z0);
+      if constexpr (kZ) {
+        tmem_st1(lane_addr + kColZ, __float_as_uint(z0));
+        put_zk(sM0, r, z0);
+      }
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -536,16 +723,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         uint32_t v[32];
         tmem_ld32(lane_addr + kColS + (uint32_t)cc, v);
         tmem_ld_wait();
-        uint32_t p[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          p[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
-        uint8_t* atom = sSb + (cc >= 64 ? kAtom : 0);
-        const int col = cc & 63;
+        for (int g = 0; g < 4; ++g) {
+          float f8[8];
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          *reinterpret_cast<uint4*>(atom + sw128_offset(r, col + 8 * g)) =
-              make_uint4(p[4 * g], p[4 * g + 1], p[4 * g + 2], p[4 * g + 3]);
+          for (int e = 0; e < 8; ++e) f8[e] = __uint_as_float(v[8 * g + e]);
+          put_sb8<kRaw>(sSb, sSbLo, r, cc + 8 * g, f8);
+        }
         if (sout) {
           float4* dst = reinterpret_cast<float4*>(args.S + (bh * D + r) * D + cc);
 #pragma unroll
@@ -554,12 +738,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
                                  __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
         }
       }
-      uint32_t zraw;
-      tmem_ld1(lane_addr + kColZ, zraw);
-      tmem_ld_wait();
-      const float zf = __uint_as_float(zraw);
-      put_zk(sM0, r, zf);
-      if (sout) args.z[bh * D + r] = zf;
+      if constexpr (kZ) {
+        uint32_t zraw;
+        tmem_ld1(lane_addr + kColZ, zraw);
+        tmem_ld_wait();
+        const float zf = __uint_as_float(zraw);
+        put_zk(sM0, r, zf);
+        if (!kRaw && sout) args.z[bh * D + r] = zf;
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -580,24 +766,85 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       ok = warp_wait(&bars[kBarO], par);
       if (!ok) break;
       tc_fence_after();
-      uint32_t dz0, dz1, rsr;
-      tmem_ld2(lane_addr + kColDz, dz0, dz1);
-      tmem_ld1(lane_addr + kColRs + par, rsr);
-      tmem_ld_wait();
-      const float inv =
-          1.f / (__uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps);
+      const int t_tok = chunk_t0(i) + r;
+      float inv = 1.f;
+      if constexpr (!kRaw) {
+        uint32_t dz0, dz1, rsr;
+        tmem_ld2(lane_addr + kColDz, dz0, dz1);
+        tmem_ld1(lane_addr + kColRs + par, rsr);
+        tmem_ld_wait();
+        const float den = __uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps;
+        inv = 1.f / den;
+        if (args.den_out != nullptr && t_tok < args.T)
+          args.den_out[((int64_t)b * args.T + t_tok) * args.H + h] = den;
+      }
       // Stage the normalised rows in this chunk's Q tile (its last readers,
       // MMA1/MMA2/MMA2b, completed before barO) ...
       const int st = i & 1;
       uint8_t* stg = sQ + st * kTile;
+      const bool affine = (MODE == kScanRowAdd || MODE == kScanRevCol) && args.vec != nullptr;
+      if (MODE == kScanNormal && args.grad_rows != nullptr) {
+        // backward's forward pass: dden = -(bf16(g / den) . out), out in fp32
+        const bool live = t_tok < args.T;
+        const int64_t row = ((int64_t)b * args.T + (live ? t_tok : 0)) * args.H + h;
+        const __nv_bfloat16* grow = args.grad_rows + row * D;
+        float acc = 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < D; cc += 64) {
-        uint32_t va[32], vb[32];
-        tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
-        tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
+        for (int cc = 0; cc < D; cc += 64) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
+          tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
+          tmem_ld_wait();
+          acc += dden_dot_32(va, inv, grow + cc);
+          acc += dden_dot_32(vb, inv, grow + cc + 32);
+          if (!args.skip_out) {
+            stage_scaled_32(va, inv, stg, r, cc);
+            stage_scaled_32(vb, inv, stg, r, cc + 32);
+          }
+        }
+        if (live) args.dden_out[row] = -acc;
+      } else if (!affine) {
+#pragma unroll 1
+        for (int cc = 0; cc < D; cc += 64) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
+          tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
+          tmem_ld_wait();
+          stage_scaled_32(va, inv, stg, r, cc);
+          stage_scaled_32(vb, inv, stg, r, cc + 32);
+        }
+      } else if constexpr (MODE == kScanRowAdd || MODE == kScanRevCol) {
+        const bool live = t_tok < args.T;
+        const int64_t row = ((int64_t)b * args.T + t_tok) * args.H + h;
+        const float coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
+        const float scale = (args.row_scale != nullptr && live) ? __bfloat162float(args.row_scale[row]) : 1.f;
+        const float* vec = args.vec + ((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * D;
+        const bool dot = args.dot_out != nullptr && live;
+        const __nv_bfloat16* drow = dot ? args.dot_rows + row * D : nullptr;
+        // centring: sigma = sum of this row's kept q'.k' + term over every
+        // chunk so far = rs (this chunk) + q'.z (earlier chunks)
+        uint32_t dz0, dz1, rsr;
+        tmem_ld2(lane_addr + kColDz, dz0, dz1);
+        tmem_ld1(lane_addr + kColRs + par, rsr);
         tmem_ld_wait();
-        stage_scaled_32(va, inv, stg, r, cc);
-        stage_scaled_32(vb, inv, stg, r, cc + 32);
+        const float sig = __uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1));
+        const float* mv = args.mvec != nullptr ? args.mvec + (int64_t)bh_idx * D : nullptr;
+        float acc = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < D; cc += 64) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
+          tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
+          tmem_ld_wait();
+          if (dot) {
+            acc += stage_affine_32<true>(va, coef, vec, sig, mv, scale, drow, stg, r, cc);
+            acc += stage_affine_32<true>(vb, coef, vec, sig, mv, scale, drow, stg, r, cc + 32);
+          } else {
+            stage_affine_32<false>(va, coef, vec, sig, mv, scale, drow, stg, r, cc);
+            stage_affine_32<false>(vb, coef, vec, sig, mv, scale, drow, stg, r, cc + 32);
+          }
+        }
+        if (dot) args.dot_out[row] = __float2bfloat16_rn(acc);
       }
       tc_fence_before();
       __syncwarp();
@@ -606,8 +853,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        const int t0 = (c0 + i) * C + 32 * q4;
-        if (t0 < args.T) {
+        const int t0 = chunk_t0(i) + 32 * q4;
+        if (t0 < args.T && !args.skip_out) {
           for (int a = 0; a < 2; ++a)
             tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
           bulk_commit_group();
@@ -899,10 +1146,28 @@ size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
   return (size_t)(B * H) * (size_t)G * (size_t)kStateFloats * sizeof(float);
 }
 
-cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
-                              void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
-                              unsigned flags, void* workspace, size_t workspace_bytes, int sms,
-                              cudaStream_t stream, int* status, bool* encoded, int64_t in_row_elems) {
+template <int MODE>
+static cudaError_t launch_main(const CUtensorMap& mQ, const CUtensorMap& mK, const CUtensorMap& mV,
+                               const CUtensorMap& mO, const ScanArgs& a, int64_t ctas,
+                               cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(scan_sm100_kernel<MODE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  scan_sm100_kernel<MODE><<<(unsigned)ctas, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, a);
+  return cudaGetLastError();
+}
+
+static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v, const void* temp,
+                                    void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                                    unsigned flags, const ScanBackwardArgs* m, void* workspace,
+                                    size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
+                                    bool* encoded, int64_t in_row_elems) {
+  const int mode = m != nullptr ? m->mode : kScanNormal;
+  if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr)) {
+    *encoded = true;
+    return cudaErrorInvalidValue;
+  }
   CUtensorMap mQ, mK, mV, mO;
   const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems) &&
                   make_map_bthd(&mK, k, B, T, H, C, in_row_elems) &&
@@ -911,7 +1176,7 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   const int64_t nchunks = (T + C - 1) / C;
-  int G = scan_sm100_segments(B, T, H, sms);
+  int G = mode == kScanNormal ? scan_sm100_segments(B, T, H, sms) : 1;
   const size_t need = scan_sm100_workspace_bytes(B, T, H, sms);
   // Without room for the segment records the scan runs one CTA per sequence.
   if (G > 1 && (workspace == nullptr || workspace_bytes < need ||
@@ -952,12 +1217,41 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
   a.seg_chunks = seg_chunks;
   a.flags = flags;
   a.status = status;
-  cudaError_t e = cudaFuncSetAttribute(scan_sm100_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
-  scan_sm100_kernel<<<(unsigned)(B * H * G), kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, a);
-  return cudaGetLastError();
+  a.add = m ? m->add : nullptr;
+  a.den_out = m ? m->den_out : nullptr;
+  a.state_in_T = m ? m->state_in_T : 0;
+  a.vec = m ? m->vec : nullptr;
+  a.row_scale = m ? static_cast<const __nv_bfloat16*>(m->row_scale) : nullptr;
+  a.dot_rows = m ? static_cast<const __nv_bfloat16*>(m->dot_rows) : nullptr;
+  a.dot_out = m ? static_cast<__nv_bfloat16*>(m->dot_out) : nullptr;
+  a.grad_rows = m ? static_cast<const __nv_bfloat16*>(m->grad_rows) : nullptr;
+  a.mvec = m ? m->mvec : nullptr;
+  a.dden_out = m ? m->dden_out : nullptr;
+  a.skip_out = m ? m->skip_out : 0;
+  const int64_t ctas = B * H * G;
+  switch (mode) {
+    case kScanRowAdd: return launch_main<kScanRowAdd>(mQ, mK, mV, mO, a, ctas, stream);
+    case kScanRevRaw: return launch_main<kScanRevRaw>(mQ, mK, mV, mO, a, ctas, stream);
+    case kScanRevCol: return launch_main<kScanRevCol>(mQ, mK, mV, mO, a, ctas, stream);
+    default: return launch_main<kScanNormal>(mQ, mK, mV, mO, a, ctas, stream);
+  }
+}
+
+cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
+                              void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                              unsigned flags, void* workspace, size_t workspace_bytes, int sms,
+                              cudaStream_t stream, int* status, bool* encoded, int64_t in_row_elems) {
+  return launch_scan_impl(q, k, v, temp, out, S, z, B, T, H, flags, nullptr, workspace,
+                          workspace_bytes, sms, stream, status, encoded, in_row_elems);
+}
+
+cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, const void* temp,
+                                   void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
+                                   unsigned flags, const ScanBackwardArgs& m, void* workspace,
+                                   size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
+                                   bool* encoded) {
+  return launch_scan_impl(q, k, v, temp, out, S, z, B, T, H, flags, &m, workspace, workspace_bytes,
+                          sms, stream, status, encoded, 0);
 }
 
 }  // namespace fakla

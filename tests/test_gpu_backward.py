@@ -87,6 +87,36 @@ def test_attention_backward_bf16(cuda):
         assert rel_l2(to_np(t.grad), e) < BF16_REL_L2, name
 
 
+@pytest.mark.parametrize("B,T,H,temp,state,final", [
+    (1, 300, 3, True, True, True),     # ragged last chunk, every gradient
+    (2, 129, 2, False, True, False),   # one token past a chunk, no temperature
+    (1, 1, 2, True, True, True),       # a single token
+    (1, 700, 2, True, False, True),    # six chunks, final-state gradients only
+    (1, 128, 1, False, False, False),  # exactly one chunk
+])
+def test_attention_backward_bf16_chunked(cuda, B, T, H, temp, state, final):
+    """bf16 128x128 heads take the tensor-core backward (chunked scans):
+    every gradient, including those of the initial state, against the
+    float64 oracle."""
+    from pulsartecture_b200.backend.interface import fa_kla_attention_with_state
+
+    D = 128
+    args = _inputs(B, T, H, D, D, torch.bfloat16, cuda, 50 + T, temp, state)
+    weights = _loss_weights(B, T, H, D, D, 60 + T)
+    q, k, v, tp, S0, z0 = args
+    out, (S, z) = fa_kla_attention_with_state(q, k, v, tp, None if S0 is None else (S0, z0), True)
+    Ro, RS, Rz = [w.float().to(cuda) for w in weights]
+    loss = (out.float() * Ro).sum()
+    if final:
+        loss = loss + (S * RS).sum() + (z * Rz).sum()
+    loss.backward()
+    exp = _oracle_grads(args, weights, final)
+    for name, t, e in zip(["q", "k", "v", "temp", "S0", "z0"], args, exp):
+        if t is None:
+            continue
+        assert rel_l2(to_np(t.grad), e) < BF16_REL_L2, name
+
+
 def test_phi_backward_kernel(cuda):
     from pulsartecture_b200 import _lib
 
