@@ -82,9 +82,9 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
 // normalised forward (optionally writing den (B,T,H) and dden), 1 unnormalised causal with a per-row term `add` added to the kept q.k
 // products, 2 unnormalised reversed (suffix state; s >= t kept), 3 as 2 with
 // a per-column term. Epilogue of modes 1 and 3: out = (o + coef * vec[chunk]
-// + sigma_t mvec) * row_scale, coef = add[t] (mode 1) or 1 (mode 3), sigma_t =
-// the sum of row t's kept q'.k' + term over all chunks so far; dot_out[t] =
-// sum over d of the unscaled row times dot_rows[t]. state_in_T: S (with
+// + sigma_t mvec) * row_scale, coef = add[t] (mode 1) or 1 (mode 3), sigma_t
+// (mode 1 with mvec) = the sum of row t's kept q'.k' + term over all chunks so
+// far; dot_out[t] = sum over d of the unscaled row times dot_rows[t]. state_in_T: S (with
 // FAKLA_STATE_IN) holds the initial state transposed. Modes 1-3 run one CTA
 // per sequence, without temp.
 struct ScanBackwardArgs {
@@ -92,15 +92,15 @@ struct ScanBackwardArgs {
   const float* add;
   float* den_out;
   int state_in_T;
-  const float* vec;
-  const float* mvec;  // modes 1, 3: v' was centred by this (B*H, D) vector
+  const float* vec;   // modes 1, 3: required
+  const float* mvec;  // mode 1: v' was centred by this (B*H, D) vector, or null
   const void* row_scale;
   const void* dot_rows;
   void* dot_out;  // bf16
-  // mode 0: dden_out[t] = -(bf16(grad_rows[t] / den_t) . out_t); skip_out: no output rows
+  // mode 0 with grad_rows: dden_out[t] = -(bf16(grad_rows[t] / den_t) . out_t),
+  // and no output rows are stored (out is not used)
   const void* grad_rows;
   float* dden_out;
-  int skip_out;
 };
 cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, const void* temp,
                                    void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,

@@ -6,29 +6,30 @@
 // zb_c = z_0 + sum of k~ over the tokens before chunk c and
 // W_c = dz_T + sum of dden_t q_t over the tokens after chunk c:
 //
-//   1. sums of k~ per chunk  -> zb (prefix), m_k = mean of k~
-//   2. forward scan (mode 0) -> den_t, and dden_t from its fp32 output
-//   3. sums of dden q and q per chunk -> W (suffix), dz_0, m_q = mean of q
-//   4. prep                  dnum, k~, k~ - m_k, q - m_q (bf16)
-//   5. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m_k) with dden_t
-//            added to row t of q'k'^T, initial state S_0^T;
-//            epilogue + dden_t zb_c + sigma_t m_k
-//   6. dk~ = reversed scan of (q' = v, k' = dnum, v' = q - m_q) with dden_t
-//            added to column t, initial state dS_T^T;
-//            epilogue + W_c + sigma_s m_q, times temp_s -> dk; dtemp_s = dk~_s . k_s
+//   1. sums of k~ per chunk  -> zb (prefix), m = mean of k~; k~ (bf16) with temp
+//   2. forward scan (mode 0) of (q, k~, v) -> den_t, and dden_t from its fp32 output
+//   3. sums of dden q per chunk -> W (suffix), dz_0
+//   4. prep                  dnum, and with temp k~ - m (bf16)
+//   5. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m) with dden_t added
+//            to row t of q'k'^T, initial state S_0^T; epilogue + dden_t zb_c
+//            + sigma_t m, sigma_t = the sum of row t of (q'k'^T + dden) over
+//            every key so far (the chunk's row sum + q'.z', z' = sum of v)
+//   6. dk~ = reversed scan of (q' = v, k' = dnum, v' = q) with dden_t added
+//            to column t, initial state dS_T^T; epilogue + W_c, times temp_s
+//            -> dk; dtemp_s = dk~_s . k_s
 //   7. dv  = reversed scan of (q' = k~, k' = q, v' = dnum), initial state
 //            dS_T; its final state is dS_0
-// sigma_t is the sum of row t of (q'k'^T + term) over every key so far; the
-// scans form it from the chunk's row sum and q'.z' (z' = sum of k' rows).
 //
 // Precision: for positive feature maps the products behind dq and dk~ cancel
 // along the features' common direction (sum_s c_ts k~_s with sum_s w_s c_ts
-// = 0). The cancelling parts are therefore kept out of bf16: dden is formed
-// from the same bf16 dnum the scans multiply with (dden_t = -bf16(dnum_t) .
-// out_t, out_t in fp32), v' is centred so that only the small deviations
-// k~ - m_k (q - m_q) are rounded while the common part m enters in fp32 through
-// sigma and the exact zb / W, and the unnormalised scans carry their state as
-// bf16 hi + lo.
+// = 0), so rounding the operands there would be amplified. Hence dden is
+// formed from the same bf16 dnum the scans multiply with (dden_t =
+// -bf16(dnum_t) . out_t, out_t in fp32); the unnormalised scans carry their
+// state as bf16 hi + lo; and where an operand is not an exact bf16 input
+// (k~ = k temp in dq) it enters centred, so that only the small deviations
+// k~ - m are rounded while the common part m is added in fp32 (sigma, zb).
+// Without temp, v' = k is exact and is not centred; dk~ multiplies the exact
+// q and needs no centring.
 //
 // Every intermediate is (B, T, H, .) like the inputs, so the scans take
 // them through the same tensor maps as the forward.
@@ -68,22 +69,17 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
 }
 
 // One (b, t, h) row per 16 threads (8 values each): dnum = bf16(dout / den)
-// (rounded as the forward scan's dden epilogue rounds it), k~ = k temp (when
-// kt is given), kc = k~ - m_k, qc = q - m_q (m per sequence (b, h)).
+// (rounded as the forward scan's dden epilogue rounds it); with temp also
+// kc = k~ - m (k~ = k temp in fp32; m per sequence (b, h)).
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
-                                const float* __restrict__ den, const __nv_bfloat16* __restrict__ q,
-                                const __nv_bfloat16* __restrict__ k,
-                                const __nv_bfloat16* __restrict__ temp,
-                                const float* __restrict__ mk, const float* __restrict__ mq,
-                                __nv_bfloat16* __restrict__ dnum, __nv_bfloat16* __restrict__ kt,
-                                __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ qc,
+                                const float* __restrict__ den, const __nv_bfloat16* __restrict__ k,
+                                const __nv_bfloat16* __restrict__ temp, const float* __restrict__ m,
+                                __nv_bfloat16* __restrict__ dnum, __nv_bfloat16* __restrict__ kc,
                                 int64_t rows, int T, int H) {
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = gid >> 4;
   const int part = (int)(gid & 15);
   if (row >= rows) return;
-  const int64_t b = row / ((int64_t)T * H);
-  const int64_t bh = b * H + row % H;
   const int64_t off = row * D + part * 8;
   float g[8];
   load8(dout + off, g);
@@ -91,61 +87,57 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
 #pragma unroll
   for (int e = 0; e < 8; ++e) g[e] *= inv;
   store8(dnum + off, g);
-  const float tv = temp != nullptr ? __bfloat162float(temp[row]) : 1.f;
-  float kv[8], m[8];
-  load8(k + off, kv);
+  if (temp != nullptr) {
+    const int64_t bh = (row / ((int64_t)T * H)) * H + row % H;
+    const float tv = __bfloat162float(temp[row]);
+    float kv[8];
+    load8(k + off, kv);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) kv[e] *= tv;
-  if (kt != nullptr) store8(kt + off, kv);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) m[e] = mk[bh * D + part * 8 + e];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) kv[e] -= m[e];
-  store8(kc + off, kv);
-  float qv[8];
-  load8(q + off, qv);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) qv[e] -= mq[bh * D + part * 8 + e];
-  store8(qc + off, qv);
+    for (int e = 0; e < 8; ++e) kv[e] = kv[e] * tv - m[bh * D + part * 8 + e];
+    store8(kc + off, kv);
+  }
 }
 
-// Per chunk c of sequence bh, 128 threads (one per feature f):
-//   s1[bh][c][f] = sum over the chunk's tokens t of w1_t x_t[f]   (w1 = 1 if null)
-//   s2[bh][c][f] = sum of x_t[f]                                  (if s2 given)
-// Grid (nchunks, B*H).
+// s[bh][c][f] = sum over the tokens t of chunk c of w_t x_t[f], w = wf (fp32),
+// else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t). Grid (nchunks,
+// B*H), 256 threads: 16 per token row (8 features each, 16-byte loads) over
+// 16 tokens at a time, then a shared memory reduction over the 16 token slots.
 __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
-                                      const float* __restrict__ w1f,
-                                      const __nv_bfloat16* __restrict__ w1h,
-                                      float* __restrict__ s1, float* __restrict__ s2, int T, int H) {
+                                      const float* __restrict__ wf,
+                                      const __nv_bfloat16* __restrict__ wh, float* __restrict__ s,
+                                      __nv_bfloat16* __restrict__ wx, int T, int H) {
+  __shared__ float red[16][D + 4];
   const int c = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
-  const int f = threadIdx.x;
-  const int t0 = c * C;
-  const int t1 = min(T, t0 + C);
-  float a0 = 0.f, a1 = 0.f, u0 = 0.f, u1 = 0.f;
-  auto w1 = [&](int64_t r) {
-    return w1f != nullptr ? w1f[r] : (w1h != nullptr ? __bfloat162float(w1h[r]) : 1.f);
-  };
-  int t = t0;
-  for (; t + 1 < t1; t += 2) {
-    const int64_t r0 = ((int64_t)b * T + t) * H + h;
-    const int64_t r1 = r0 + H;
-    const float x0 = __bfloat162float(x[r0 * D + f]), x1 = __bfloat162float(x[r1 * D + f]);
-    a0 = fmaf(w1(r0), x0, a0);
-    a1 = fmaf(w1(r1), x1, a1);
-    u0 += x0;
-    u1 += x1;
+  const int part = threadIdx.x & 15;  // features 8 part .. 8 part + 7
+  const int slot = threadIdx.x >> 4;  // token slot
+  const int t1 = min(T, c * C + C);
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int t = c * C + slot; t < t1; t += 16) {
+    const int64_t r = ((int64_t)b * T + t) * H + h;
+    const float w = wf != nullptr ? wf[r] : (wh != nullptr ? __bfloat162float(wh[r]) : 1.f);
+    float xv[8];
+    load8(x + r * D + part * 8, xv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, xv[e], acc[e]);
+    if (wx != nullptr) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xv[e] *= w;
+      store8(wx + r * D + part * 8, xv);
+    }
   }
-  if (t < t1) {
-    const int64_t r0 = ((int64_t)b * T + t) * H + h;
-    const float x0 = __bfloat162float(x[r0 * D + f]);
-    a0 = fmaf(w1(r0), x0, a0);
-    u0 += x0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[slot][part * 8 + e] = acc[e];
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v += red[i][threadIdx.x];
+    s[((int64_t)bh * gridDim.x + c) * D + threadIdx.x] = v;
   }
-  const int64_t o = ((int64_t)bh * gridDim.x + c) * D + f;
-  s1[o] = a0 + a1;
-  if (s2 != nullptr) s2[o] = u0 + u1;
 }
 
 // Exclusive prefix over the chunks (in place): s[c] <- init + sum_{c' < c} s[c'],
@@ -170,7 +162,7 @@ __global__ void bwd_scan_chunks_kernel(float* __restrict__ s, const float* __res
 }
 
 struct BwdLayout {
-  size_t den, zb, dnum, dden, kt, kc, qc, wq, sq, mk, mq, scan, total;
+  size_t den, dden, dnum, kt, kc, zb, wq, mk, scan, total;
 };
 
 BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
@@ -184,13 +176,10 @@ BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
   l.dden = o; o += up(rows * 4);
   l.dnum = o; o += up(rows * D * 2);
   l.kt = o;   o += temp ? up(rows * D * 2) : 0;
-  l.kc = o;   o += up(rows * D * 2);
-  l.qc = o;   o += up(rows * D * 2);
+  l.kc = o;   o += temp ? up(rows * D * 2) : 0;
   l.zb = o;   o += chunk_vecs;
   l.wq = o;   o += chunk_vecs;
-  l.sq = o;   o += chunk_vecs;
   l.mk = o;   o += up((size_t)(B * H) * D * 4);
-  l.mq = o;   o += up((size_t)(B * H) * D * 4);
   l.scan = o; o += up(scan_sm100_workspace_bytes(B, T, H, sms));
   l.total = o;
   return l;
@@ -204,7 +193,7 @@ bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_
 }
 
 size_t backward_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
-  // sized for the temp case (the k~ buffer); without temp it goes unused
+  // sized for the temp case (the k~ buffers); without temp they go unused
   return bwd_layout(B, T, H, true, sms).total;
 }
 
@@ -220,13 +209,10 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   auto* dden = reinterpret_cast<float*>(ws + l.dden);
   auto* dnum = reinterpret_cast<__nv_bfloat16*>(ws + l.dnum);
   auto* kt = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kt) : nullptr;
-  auto* kc = reinterpret_cast<__nv_bfloat16*>(ws + l.kc);
-  auto* qc = reinterpret_cast<__nv_bfloat16*>(ws + l.qc);
+  auto* kc = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kc) : nullptr;
   auto* zb = reinterpret_cast<float*>(ws + l.zb);
   auto* wq = reinterpret_cast<float*>(ws + l.wq);
-  auto* sq = reinterpret_cast<float*>(ws + l.sq);
   auto* mk = reinterpret_cast<float*>(ws + l.mk);
-  auto* mq = reinterpret_cast<float*>(ws + l.mq);
   void* scan_ws = ws + l.scan;
   const size_t scan_bytes = l.total - l.scan;
   const int64_t rows = B * T * H;
@@ -237,53 +223,52 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   const auto* th = static_cast<const __nv_bfloat16*>(temp);
   cudaError_t e;
 
-  // 1. zb (z before each chunk, from z_0) and m_k: sums of k~ per chunk
-  bwd_chunk_sums_kernel<<<cgrid, D, 0, stream>>>(kh, nullptr, th, zb, nullptr, (int)T, (int)H);
+  // 1. zb (z before each chunk, from z_0) and the mean of k~
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, (int)T, (int)H);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(zb, z0, nullptr, mk, nch, (int)T, 0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-  // 2. forward: den and dden (no output rows: dq only names a valid tensor
-  // for the output map)
+  // 2. forward: den and dden (no output rows)
   ScanBackwardArgs m{};
   m.mode = 0;
   m.den_out = den;
   m.grad_rows = dout;
   m.dden_out = dden;
-  m.skip_out = 1;
   const unsigned in0 = S0 != nullptr ? FAKLA_STATE_IN : 0u;
-  e = launch_scan_sm100_mode(q, k, v, temp, dq, const_cast<float*>(S0), const_cast<float*>(z0), B,
-                             T, H, in0, m, scan_ws, scan_bytes, sms, stream, status, encoded);
+  // k~ is precomputed: the scan then skips its in-tile temp scaling, which
+  // the P warps would otherwise do on the critical path of every chunk
+  const void* ktil = temp != nullptr ? (const void*)kt : k;
+  e = launch_scan_sm100_mode(q, ktil, v, nullptr, nullptr, const_cast<float*>(S0),
+                             const_cast<float*>(z0), B, T, H, in0, m, scan_ws, scan_bytes, sms,
+                             stream, status, encoded);
   if (e != cudaSuccess) return e;
 
-  // 3. W (suffix sums of dden q from dz_T), dz_0, m_q
-  bwd_chunk_sums_kernel<<<cgrid, D, 0, stream>>>(qh, dden, nullptr, wq, sq, (int)T, (int)H);
+  // 3. W (suffix sums of dden q from dz_T) and dz_0
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, (int)T, (int)H);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(wq, dz_final, dz0, nullptr, nch,
                                                               (int)T, 1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(sq, nullptr, nullptr, mq, nch,
-                                                              (int)T, 0);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-  // 4. dnum, k~, k~ - m_k, q - m_q
+  // 4. dnum (and with temp k~ - m)
   {
     const int64_t threads = rows * 16;
     bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)dout, den, qh, kh, th, mk, mq, dnum, kt, kc, qc, rows, (int)T, (int)H);
+        (const __nv_bfloat16*)dout, den, kh, th, mk, dnum, kc, rows, (int)T, (int)H);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  const void* ktil = temp != nullptr ? (const void*)kt : k;
 
   // 5. dq
   m = ScanBackwardArgs{};
   m.mode = 1;
   m.add = dden;
   m.vec = zb;
-  m.mvec = mk;
+  m.mvec = temp != nullptr ? mk : nullptr;
   m.state_in_T = 1;
-  e = launch_scan_sm100_mode(dnum, v, kc, nullptr, dq, const_cast<float*>(S0), nullptr, B, T, H,
-                             in0, m, nullptr, 0, sms, stream, status, encoded);
+  e = launch_scan_sm100_mode(dnum, v, temp != nullptr ? (const void*)kc : k, nullptr, dq,
+                             const_cast<float*>(S0), nullptr, B, T, H, in0, m, nullptr, 0, sms,
+                             stream, status, encoded);
   if (e != cudaSuccess) return e;
 
   // 6. dk (and dtemp); before dv, whose final state may overwrite dS_T in place
@@ -291,7 +276,6 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m.mode = 3;
   m.add = dden;
   m.vec = wq;
-  m.mvec = mq;
   m.state_in_T = 1;
   m.row_scale = temp;
   if (temp != nullptr && dtemp != nullptr) {
@@ -299,7 +283,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
     m.dot_out = dtemp;
   }
   const unsigned fk = dS_final != nullptr ? FAKLA_STATE_IN : 0u;
-  e = launch_scan_sm100_mode(v, dnum, qc, nullptr, dk, const_cast<float*>(dS_final), nullptr, B, T,
+  e = launch_scan_sm100_mode(v, dnum, q, nullptr, dk, const_cast<float*>(dS_final), nullptr, B, T,
                              H, fk, m, nullptr, 0, sms, stream, status, encoded);
   if (e != cudaSuccess) return e;
 

@@ -101,7 +101,8 @@ enum Bar {
   kKReady,
   kDrain,
   kKFree,   // unnormalised modes: the single K tile read by MMA4
-  kNumBars
+  kRow0,    // (4) per output warp: its 32 rows of the epilogue's row tensor landed
+  kNumBars = kRow0 + 4
 };
 static_assert(kNumBars * 8 + 8 <= kHeadBytes, "barrier area");
 
@@ -116,9 +117,8 @@ struct ScanArgs {
   unsigned flags;
   int* status;
   // backward passes (modes below)
-  const __nv_bfloat16* grad_rows;  // kScanNormal: (B,T,H,D) output gradient -> dden_out, or null
+  const __nv_bfloat16* grad_rows;  // kScanNormalGrad: (B,T,H,D) output gradient -> dden_out (no output rows)
   float* dden_out;                 // (B,T,H): -(bf16(g/den) . out) (g = grad_rows)
-  int skip_out;                    // do not store the output rows
   const float* add;           // (B,T,H) per-token term added to the kept P entries, or null
   float* den_out;             // (B,T,H) denominators of the normalised mode, or null
   int state_in_T;             // the initial state is given transposed (S[dv][f])
@@ -137,11 +137,12 @@ struct ScanArgs {
 // scans of the same shape as the forward one (simt_backward.cu gives the
 // formulas; sm100_backward.cu runs them):
 //   kScanNormal  out = (q S_{<c} + (M o Q K^T) V) / den        (the forward)
+//   kScanNormalGrad  the forward, also writing den and dden (backward's first pass)
 //   kScanRowAdd  out = q S_{<c} + (M o (Q K^T + a 1^T)) V       (dq: a = dden)
 //   kScanRevRaw  out = q S_{>c} + (M' o Q K^T) V                (dv, reversed time)
 //   kScanRevCol  out = q S_{>c} + (M' o (Q K^T + 1 b^T)) V      (dk~, reversed: b = dden)
 // M keeps s <= t; M' keeps s >= t and the chunks are walked from the end.
-enum { kScanNormal = 0, kScanRowAdd = 1, kScanRevRaw = 2, kScanRevCol = 3 };
+enum { kScanNormal = 0, kScanRowAdd = 1, kScanRevRaw = 2, kScanRevCol = 3, kScanNormalGrad = 4 };
 
 __device__ __forceinline__ uint64_t kdesc(uint32_t tile_addr, int j) {
   // K-major operand, K step j (16 elements): atom j/4, +32 B per step inside.
@@ -170,18 +171,24 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
-// k~ = k * temp on row r (one token) of a K tile in shared memory.
+// k~ = k * temp on row r (one token) of a K tile in shared memory. Rows are
+// 128 bytes (all 32 banks), so the 16-byte pieces are visited in an order
+// rotated by the row: the 32 rows of a warp then touch 8 different bank
+// groups per access instead of one.
 __device__ __forceinline__ void scale_k_row(uint8_t* tK, int r, float tv) {
+  const __nv_bfloat162 t2 = __floats2bfloat162_rn(tv, tv);
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
+    for (int c = 0; c < 8; ++c) {
+      const int ch = (c + r) & 7;
       uint4* p = reinterpret_cast<uint4*>(tK + a * kAtom + r * 128 + ch * 16);
       uint4 u = *p;
-      float f[8];
-      bf16x8_to_f32(u, f);
-      u = make_uint4(pack_bf16x2(f[0] * tv, f[1] * tv), pack_bf16x2(f[2] * tv, f[3] * tv),
-                     pack_bf16x2(f[4] * tv, f[5] * tv), pack_bf16x2(f[6] * tv, f[7] * tv));
+      // bf16 pair products, rounded once (tv is a bf16 value): the same bits
+      // as rounding the fp32 product k * temp
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __hmul2(h[e], t2);
       *p = u;
     }
   }
@@ -210,19 +217,20 @@ __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
 // [16,32) (two tokens per column). kMask: 0 keeps the whole group, 1 keeps
 // s <= r (causal diagonal group), 2 keeps s >= r (reversed diagonal group).
 // The kept values first get `arow` (a per-row term) and bcol[s - sbase] (a
-// per-column term, held by lane s - sbase of the warp). Returns the sum of
-// the kept values.
+// per-column term: 32 floats in shared memory, the same for every row).
+// Returns the sum of the kept values.
 template <int kMask, bool kCol>
 __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase, int r,
-                                             uint32_t p_addr, float arow, float bcol) {
+                                             uint32_t p_addr, float arow, const float* bcol) {
   uint32_t hi[16], lo[16];
   float rs = 0.f;
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
     float x0 = __uint_as_float(v[2 * e]) + arow, x1 = __uint_as_float(v[2 * e + 1]) + arow;
     if (kCol) {
-      x0 += __shfl_sync(0xffffffffu, bcol, 2 * e);
-      x1 += __shfl_sync(0xffffffffu, bcol, 2 * e + 1);
+      const float2 bb = reinterpret_cast<const float2*>(bcol)[e];
+      x0 += bb.x;
+      x1 += bb.y;
     }
     if (kMask == 1) {
       x0 = sbase + 2 * e <= r ? x0 : 0.f;
@@ -248,7 +256,7 @@ __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase,
 // masked. Reversed: groups above the diagonal are kept whole.
 template <bool kRev, bool kCol>
 __device__ __forceinline__ float split_group_at(const uint32_t (&v)[32], int g, int q4, int r,
-                                                uint32_t p_addr, float arow, float bcol) {
+                                                uint32_t p_addr, float arow, const float* bcol) {
   return g == q4 ? split_group<kRev ? 2 : 1, kCol>(v, 32 * g, r, p_addr, arow, bcol)
                  : split_group<0, kCol>(v, 32 * g, r, p_addr, arow, bcol);
 }
@@ -298,61 +306,69 @@ __device__ __forceinline__ void stage_scaled_32(const uint32_t (&v)[32], float i
   }
 }
 
-// sum over columns [c, c+32) of bf16(g * inv) * (x * inv): x = out * den
-// (fp32 bits in v), g = the output gradient row (bf16, global memory).
-__device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, const __nv_bfloat16* g) {
-  float acc = 0.f;
+// Half a row (64 bf16 from column c0) of a 128-row x 128-column 128B-swizzled
+// tile in shared memory.
+__device__ __forceinline__ void load_row_smem(const uint8_t* tile, int r, int c0, uint4 (&u)[8]) {
+  const uint8_t* atom = tile + (c0 >= 64 ? kAtom : 0);
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    u[k] = *reinterpret_cast<const uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((c0 & 63) + 8 * k)));
+}
+
+// sum over 32 columns of bf16(g * inv) * (x * inv): x = out * den (fp32 bits
+// in v), g = 32 bf16 of the output gradient row (4 uint4). bf16(g * inv) is
+// rounded as bf16 pairs, exactly as the dnum tensor is stored.
+__device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, const uint4* g) {
+  float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float gf[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(g + 8 * k), gf);
+    bf16x8_to_f32(g[k], gf);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float dn = __bfloat162float(__float2bfloat16_rn(gf[e] * inv));
-      acc = fmaf(dn, __uint_as_float(v[8 * k + e]) * inv, acc);
+    for (int e = 0; e < 8; e += 2) {
+      const float2 dn = __bfloat1622float2(__floats2bfloat162_rn(gf[e] * inv, gf[e + 1] * inv));
+      acc0 = fmaf(dn.x, __uint_as_float(v[8 * k + e]), acc0);
+      acc1 = fmaf(dn.y, __uint_as_float(v[8 * k + e + 1]), acc1);
     }
   }
-  return acc;
-}
-
-__device__ __forceinline__ void load_f32x8(const float* p, float (&f)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p);
-  const float4 b = *reinterpret_cast<const float4*>(p + 4);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  return (acc0 + acc1) * inv;
 }
 
 // Backward epilogue of one row: y = (x + coef * vec + sig * mv) * scale over
-// columns [col0, col0+32) (vec, mv: fp32 in global memory, the same for
-// every row of the chunk; mv may be null), written as bf16 like
-// stage_scaled_32. With kDot the return value is sum(x + coef * vec + sig *
-// mv) * drow over these columns (drow: bf16 row in global memory), else 0.
-template <bool kDot>
+// columns [col0, col0+32), written as bf16 like stage_scaled_32. vec and mv
+// (32 floats each from column col0, shared memory, the same for every row;
+// mv only with kM) are read as broadcasts. With kDot the return value is
+// sum(x + coef * vec + sig * mv) * k over these columns, k = 32 bf16 of this
+// row (4 uint4), else 0.
+template <bool kDot, bool kM>
 __device__ __forceinline__ float stage_affine_32(const uint32_t (&v)[32], float coef, const float* vec,
                                                  float sig, const float* mv, float scale,
-                                                 const __nv_bfloat16* drow, uint8_t* tile, int r,
-                                                 int col0) {
+                                                 const uint4* krow, uint8_t* tile, int r, int col0) {
   uint8_t* atom = tile + (col0 >= 64 ? kAtom : 0);
-  float dot = 0.f;
+  float dot0 = 0.f, dot1 = 0.f;
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    float wv[8], mvv[8];
-    load_f32x8(vec + col0 + 8 * g, wv);
-    if (mv != nullptr) {
-      load_f32x8(mv + col0 + 8 * g, mvv);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mvv[e] = 0.f;
-    }
+    const float4 w0 = reinterpret_cast<const float4*>(vec)[2 * g];
+    const float4 w1 = reinterpret_cast<const float4*>(vec)[2 * g + 1];
+    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     float y[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      y[e] = fmaf(sig, mvv[e], fmaf(coef, wv[e], __uint_as_float(v[8 * g + e])));
+    for (int e = 0; e < 8; ++e) y[e] = fmaf(coef, w[e], __uint_as_float(v[8 * g + e]));
+    if (kM) {
+      const float4 m0 = reinterpret_cast<const float4*>(mv)[2 * g];
+      const float4 m1 = reinterpret_cast<const float4*>(mv)[2 * g + 1];
+      const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = fmaf(sig, m[e], y[e]);
+    }
     if (kDot) {
       float kf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(drow + col0 + 8 * g), kf);
+      bf16x8_to_f32(krow[g], kf);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) dot = fmaf(y[e], kf[e], dot);
+      for (int e = 0; e < 8; e += 2) {
+        dot0 = fmaf(y[e], kf[e], dot0);
+        dot1 = fmaf(y[e + 1], kf[e + 1], dot1);
+      }
     }
     uint4 u;
     u.x = pack_bf16x2(y[0] * scale, y[1] * scale);
@@ -361,7 +377,7 @@ __device__ __forceinline__ float stage_affine_32(const uint32_t (&v)[32], float 
     u.w = pack_bf16x2(y[6] * scale, y[7] * scale);
     *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((col0 & 63) + 8 * g))) = u;
   }
-  return dot;
+  return dot0 + dot1;
 }
 
 // Warp-uniform forms of the bounded wait and of the abort check, for warps
@@ -382,7 +398,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-    const ScanArgs args) {
+    const __grid_constant__ CUtensorMap tmR, const ScanArgs args) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -413,11 +429,29 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   const int nch = c1 - c0;
   const bool has_temp = args.temp != nullptr;
   const bool last_seg = seg == args.G - 1;
-  constexpr bool kRaw = MODE != kScanNormal;     // no normaliser: q.z, z and den are not formed
-  constexpr bool kRev = MODE >= kScanRevRaw;     // chunks from the end, s >= t kept
-  // the k' row sum z (MMA4b) and q'.z (MMA2b): the normaliser of mode 0, the
-  // centring terms of modes 1 and 3
-  constexpr bool kZ = MODE != kScanRevRaw;
+  constexpr bool kGrad = MODE == kScanNormalGrad;
+  constexpr bool kRaw = MODE != kScanNormal && !kGrad;  // no normaliser: q.z, z, den not formed
+  constexpr bool kRev = MODE == kScanRevRaw || MODE == kScanRevCol;  // chunks from the end, s >= t kept
+  // the k' row sum z (MMA4b) and q'.z (MMA2b): the normaliser of the forward,
+  // the centring term of kScanRowAdd
+  constexpr bool kZ = MODE != kScanRevRaw && MODE != kScanRevCol;
+  // The epilogue's per-row tensor (the output gradient of kScanNormalGrad,
+  // the dot rows of kScanRevCol) comes by TMA into the chunk's Q tile once
+  // the MMAs have read it; kScanRevCol then stages its output in the V tile,
+  // which its output warps (not MMA3's commit) hand back to the producer.
+  constexpr bool kRowTile = kGrad || MODE == kScanRevCol;
+  constexpr bool kStageInV = MODE == kScanRevCol;
+  // Vectors shared by every row of a chunk, broadcast from shared memory in
+  // the unused rows of the two 1 KB N=16 operand atoms (with kZ, rows 0-1 of
+  // both hold ZK and rows 4-5 of M0 ONES; the other rows only feed result
+  // columns nobody reads): the epilogue's vector, the centring vector
+  // (kScanRowAdd: m[0:64] in rows 6-7 of M0, m[64:128] in rows 6-7 of M1) and
+  // the per-column terms of kScanRevCol.
+  constexpr bool kAffine = MODE == kScanRowAdd || MODE == kScanRevCol;
+  float* vec_sm = reinterpret_cast<float*>(sM0 + 1024 + (kZ ? 256 : 0));
+  float* mlo_sm = reinterpret_cast<float*>(sM0 + 768);
+  float* mhi_sm = reinterpret_cast<float*>(sM0 + 1024 + 768);
+  float* bcol_sm = reinterpret_cast<float*>(sM0);
   auto k_tile = [&](int st) { return sK + (kRaw ? 0 : st * kTile); };
   // first token of this CTA's chunk i
   auto chunk_t0 = [&](int i) {
@@ -428,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kFull0 + s], 1);
-      mbar_init(&bars[kEmpty0 + s], 1);
+      mbar_init(&bars[kEmpty0 + s], kStageInV ? 4 : 1);
       mbar_init(&bars[kEmptyQ0 + s], 4);
     }
     mbar_init(&bars[kBarP], 1);
@@ -440,12 +474,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     mbar_init(&bars[kKReady], 4);
     mbar_init(&bars[kDrain], 1);
     mbar_init(&bars[kKFree], 1);
+    for (int w = 0; w < 4; ++w) mbar_init(&bars[kRow0 + w], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmO);
+    if (kRowTile) tma_prefetch_desc(&tmR);
   }
   // ONES: rows 4-5 of M0 (256 bytes of bf16 1.0).
   if (threadIdx.x < 64)
@@ -576,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           mma_ts(tmem + kColO, tmem + col + 16u, mndesc(aV, j), idPV, 1u);
         }
         mma_commit(&bars[kBarO]);
-        mma_commit(&bars[kEmpty0 + st]);
+        if constexpr (!kStageInV) mma_commit(&bars[kEmpty0 + st]);
       }
       if (!ok) {
         report_status(args.status, FAKLA_ERR_TIMEOUT);
@@ -594,27 +630,30 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const int r = 32 * q4 + lane;  // token r of the chunk
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     bool ok = true;
-    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+    constexpr bool kCol = MODE == kScanRevCol;
+    // kScanRevCol's four P warps share the column terms through shared memory
+    // and stop together (a named barrier that ORs their wait results; every
+    // wait before it is bounded).
+    for (int i = 0; i < nch && (kCol || !warp_aborted(abort_flag)); ++i) {
       const uint32_t par = (uint32_t)i & 1u;
-      if (has_temp) {
-        const int st = i & 1;
-        ok = warp_wait(&bars[kFull0 + st], (uint32_t)(i >> 1) & 1u);
-        if (!ok) break;
-        scale_k_row(sK + st * kTile, r, temp_at(args.temp, b, args.T, args.H, h, chunk_t0(i) + r));
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kKReady]);
-      }
+      // the per-row / per-column terms, loaded before the wait so that their
+      // latency overlaps it
+      const int t0 = chunk_t0(i);
+      const float arow = MODE == kScanRowAdd ? add_at(args.add, b, args.T, args.H, h, t0 + r) : 0.f;
+      const float bval = kCol ? add_at(args.add, b, args.T, args.H, h, t0 + r) : 0.f;
       ok = warp_wait(&bars[kBarP], par);
-      if (!ok) break;
+      if constexpr (kCol) {
+        if (named_barrier_or(2, 128, !ok || *abort_flag != 0)) break;
+        bcol_sm[r] = bval;  // the previous chunk's readers passed the barrier above
+        named_barrier_sync(2, 128);
+      } else if (!ok) {
+        break;
+      }
       tc_fence_after();
       // Token groups of 32: this warp's rows are group q4, so group g is
       // whole, diagonal or empty for every lane (causal: whole below the
       // diagonal; reversed: whole above it).
       const uint32_t p_addr = lane_addr + kColP;
-      const int t0 = chunk_t0(i);
-      constexpr bool kCol = MODE == kScanRevCol;
-      const float arow = MODE == kScanRowAdd ? add_at(args.add, b, args.T, args.H, h, t0 + r) : 0.f;
       float rs = 0.f;
 #pragma unroll 1
       for (int g0 = 0; g0 < 4; g0 += 2) {
@@ -629,15 +668,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (k0) tmem_ld32(p_addr + (uint32_t)(32 * g0), va);
         if (k1) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
         tmem_ld_wait();
-        // per-column terms of tokens 32g + lane (broadcast inside split_group)
-        const float b0 = kCol ? add_at(args.add, b, args.T, args.H, h, t0 + 32 * g0 + lane) : 0.f;
-        const float b1 = kCol ? add_at(args.add, b, args.T, args.H, h, t0 + 32 * g0 + 32 + lane) : 0.f;
         if (k0)
-          rs += split_group_at<kRev, kCol>(va, g0, q4, r, p_addr, arow, b0);
+          rs += split_group_at<kRev, kCol>(va, g0, q4, r, p_addr, arow, bcol_sm + 32 * g0);
         else
           zero_group(g0, p_addr);
         if (k1)
-          rs += split_group_at<kRev, kCol>(vb, g0 + 1, q4, r, p_addr, arow, b1);
+          rs += split_group_at<kRev, kCol>(vb, g0 + 1, q4, r, p_addr, arow, bcol_sm + 32 * g0 + 32);
         else
           zero_group(g0 + 1, p_addr);
       }
@@ -711,9 +747,23 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSReady]);
     }
+    // With temp, these warps also turn the K tile of chunk j into k~ = k temp
+    // (row r each) before MMA1 reads it: between two state refreshes, while
+    // the P warps split the previous chunk, so it stays off the chunk's
+    // critical path.
+    auto scale_k = [&](int j) {
+      const int st = j & 1;
+      if (!warp_wait(&bars[kFull0 + st], (uint32_t)(j >> 1) & 1u)) return false;
+      scale_k_row(sK + st * kTile, r, temp_at(args.temp, b, args.T, args.H, h, chunk_t0(j) + r));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kKReady]);
+      return true;
+    };
     const bool write_state = last_seg && (args.flags & FAKLA_STATE_OUT) && args.S != nullptr;
     bool ok = true;
-    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+    if (has_temp && nch > 0) ok = scale_k(0);
+    for (int i = 0; ok && i < nch && !warp_aborted(abort_flag); ++i) {
       ok = warp_wait(&bars[kBarS], (uint32_t)i & 1u);
       if (!ok) break;
       tc_fence_after();
@@ -750,6 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSReady]);
+      if (has_temp && i + 1 < nch) ok = scale_k(i + 1);
     }
     if (!ok) {
       report_status(args.status, FAKLA_ERR_TIMEOUT);
@@ -760,13 +811,57 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     const int q4 = warp & 3;
     const int r = 32 * q4 + lane;  // token r of the chunk
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+    // The affine modes' four output warps share the chunk's vector (and the
+    // centring vector) through shared memory and stop together (a named
+    // barrier that ORs their wait results; every wait before it is bounded).
+    const bool centre = MODE == kScanRowAdd && args.mvec != nullptr;
+    if (kAffine) {
+      if (centre) (r < 64 ? mlo_sm[r] : mhi_sm[r - 64]) = args.mvec[(int64_t)bh_idx * D + r];
+      named_barrier_sync(1, 128);
+    }
     bool ok = true;
-    for (int i = 0; i < nch && !warp_aborted(abort_flag); ++i) {
+    for (int i = 0; i < nch && (kAffine || !warp_aborted(abort_flag)); ++i) {
       const uint32_t par = (uint32_t)i & 1u;
-      ok = warp_wait(&bars[kBarO], par);
-      if (!ok) break;
-      tc_fence_after();
       const int t_tok = chunk_t0(i) + r;
+      const int st = i & 1;
+      const bool live = t_tok < args.T;
+      const int64_t row = ((int64_t)b * args.T + (live ? t_tok : 0)) * args.H + h;
+      const bool row_tile = kGrad || (MODE == kScanRevCol && args.dot_out != nullptr);
+      bool wok = true;  // this warp's waits of the chunk
+      if (kRowTile && row_tile) {
+        // this warp's 32 rows of the row tensor into the Q tile, whose MMA
+        // readers (MMA1, MMA2, MMA2b) completed with barS
+        wok = warp_wait(&bars[kBarS], par);
+        if (wok && lane == 0) {
+          uint64_t* rb = &bars[kRow0 + q4];
+          mbar_arrive_expect_tx(rb, 32 * 128 * 2);
+          for (int a = 0; a < 2; ++a)
+            tma_load_4d(sQ + st * kTile + a * kAtom + q4 * (32 * 128), &tmR, rb, a * 64, h,
+                        chunk_t0(i) + 32 * q4, b);
+        }
+      }
+      // the chunk's vector and per-row scalars of the affine epilogues, loaded
+      // before the wait so that their latency overlaps MMA3
+      float vval = 0.f, coef = 0.f, scale = 1.f;
+      if (kAffine) {
+        vval = args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * D + r];
+        coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
+        if (args.row_scale != nullptr && live) scale = __bfloat162float(args.row_scale[row]);
+      }
+      if (wok) wok = warp_wait(&bars[kBarO], par);
+      if (wok && kRowTile && row_tile) wok = warp_wait(&bars[kRow0 + q4], par);
+      if constexpr (kAffine) {
+        if (named_barrier_or(1, 128, !wok || *abort_flag != 0)) {
+          ok = wok;
+          break;
+        }
+        vec_sm[r] = vval;  // the previous chunk's readers passed the barrier above
+        named_barrier_sync(1, 128);
+      } else if (!wok) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
       float inv = 1.f;
       if constexpr (!kRaw) {
         uint32_t dz0, dz1, rsr;
@@ -775,35 +870,31 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         tmem_ld_wait();
         const float den = __uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps;
         inv = 1.f / den;
-        if (args.den_out != nullptr && t_tok < args.T)
+        if (args.den_out != nullptr && live)
           args.den_out[((int64_t)b * args.T + t_tok) * args.H + h] = den;
       }
       // Stage the normalised rows in this chunk's Q tile (its last readers,
-      // MMA1/MMA2/MMA2b, completed before barO) ...
-      const int st = i & 1;
-      uint8_t* stg = sQ + st * kTile;
-      const bool affine = (MODE == kScanRowAdd || MODE == kScanRevCol) && args.vec != nullptr;
-      if (MODE == kScanNormal && args.grad_rows != nullptr) {
-        // backward's forward pass: dden = -(bf16(g / den) . out), out in fp32
-        const bool live = t_tok < args.T;
-        const int64_t row = ((int64_t)b * args.T + (live ? t_tok : 0)) * args.H + h;
-        const __nv_bfloat16* grow = args.grad_rows + row * D;
+      // MMA1/MMA2/MMA2b, completed before barO), or in its V tile (MMA3, the
+      // last reader, completed with barO) ...
+      uint8_t* stg = (kStageInV ? sV : sQ) + st * kTile;
+      const uint8_t* rtile = sQ + st * kTile;
+      if constexpr (kGrad) {
+        // backward's forward pass: dden = -(bf16(g / den) . out), out in fp32;
+        // no output rows
         float acc = 0.f;
 #pragma unroll 1
         for (int cc = 0; cc < D; cc += 64) {
+          uint4 rh[8];
+          load_row_smem(rtile, r, cc, rh);
           uint32_t va[32], vb[32];
           tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
           tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
           tmem_ld_wait();
-          acc += dden_dot_32(va, inv, grow + cc);
-          acc += dden_dot_32(vb, inv, grow + cc + 32);
-          if (!args.skip_out) {
-            stage_scaled_32(va, inv, stg, r, cc);
-            stage_scaled_32(vb, inv, stg, r, cc + 32);
-          }
+          acc += dden_dot_32(va, inv, rh);
+          acc += dden_dot_32(vb, inv, rh + 4);
         }
         if (live) args.dden_out[row] = -acc;
-      } else if (!affine) {
+      } else if (!kAffine) {
 #pragma unroll 1
         for (int cc = 0; cc < D; cc += 64) {
           uint32_t va[32], vb[32];
@@ -813,38 +904,38 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           stage_scaled_32(va, inv, stg, r, cc);
           stage_scaled_32(vb, inv, stg, r, cc + 32);
         }
-      } else if constexpr (MODE == kScanRowAdd || MODE == kScanRevCol) {
-        const bool live = t_tok < args.T;
-        const int64_t row = ((int64_t)b * args.T + t_tok) * args.H + h;
-        const float coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
-        const float scale = (args.row_scale != nullptr && live) ? __bfloat162float(args.row_scale[row]) : 1.f;
-        const float* vec = args.vec + ((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * D;
-        const bool dot = args.dot_out != nullptr && live;
-        const __nv_bfloat16* drow = dot ? args.dot_rows + row * D : nullptr;
-        // centring: sigma = sum of this row's kept q'.k' + term over every
-        // chunk so far = rs (this chunk) + q'.z (earlier chunks)
-        uint32_t dz0, dz1, rsr;
-        tmem_ld2(lane_addr + kColDz, dz0, dz1);
-        tmem_ld1(lane_addr + kColRs + par, rsr);
-        tmem_ld_wait();
-        const float sig = __uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1));
-        const float* mv = args.mvec != nullptr ? args.mvec + (int64_t)bh_idx * D : nullptr;
+      } else if constexpr (kAffine) {
+        // centring (kScanRowAdd): sigma = sum of this row's kept q'.k' + term
+        // over every chunk so far = rs (this chunk) + q'.z (earlier chunks)
+        float sig = 0.f;
+        if constexpr (kZ) {
+          uint32_t dz0, dz1, rsr;
+          tmem_ld2(lane_addr + kColDz, dz0, dz1);
+          tmem_ld1(lane_addr + kColRs + par, rsr);
+          tmem_ld_wait();
+          sig = __uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1));
+        }
+        if (!centre) sig = 0.f;
+        constexpr bool kDot = MODE == kScanRevCol;
         float acc = 0.f;
 #pragma unroll 1
         for (int cc = 0; cc < D; cc += 64) {
+          uint4 rh[8];
+          if (kDot && row_tile) load_row_smem(rtile, r, cc, rh);
           uint32_t va[32], vb[32];
           tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
           tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
           tmem_ld_wait();
-          if (dot) {
-            acc += stage_affine_32<true>(va, coef, vec, sig, mv, scale, drow, stg, r, cc);
-            acc += stage_affine_32<true>(vb, coef, vec, sig, mv, scale, drow, stg, r, cc + 32);
+          const float* mv = cc < 64 ? mlo_sm + cc : mhi_sm + (cc - 64);
+          if (kDot && row_tile) {
+            acc += stage_affine_32<true, kZ>(va, coef, vec_sm + cc, sig, mv, scale, rh, stg, r, cc);
+            acc += stage_affine_32<true, kZ>(vb, coef, vec_sm + cc + 32, sig, mv + 32, scale, rh + 4, stg, r, cc + 32);
           } else {
-            stage_affine_32<false>(va, coef, vec, sig, mv, scale, drow, stg, r, cc);
-            stage_affine_32<false>(vb, coef, vec, sig, mv, scale, drow, stg, r, cc + 32);
+            stage_affine_32<false, kZ>(va, coef, vec_sm + cc, sig, mv, scale, rh, stg, r, cc);
+            stage_affine_32<false, kZ>(vb, coef, vec_sm + cc + 32, sig, mv + 32, scale, rh + 4, stg, r, cc + 32);
           }
         }
-        if (dot) args.dot_out[row] = __float2bfloat16_rn(acc);
+        if (kDot && row_tile && live) args.dot_out[row] = __float2bfloat16_rn(acc);
       }
       tc_fence_before();
       __syncwarp();
@@ -854,13 +945,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       __syncwarp();
       if (lane == 0) {
         const int t0 = chunk_t0(i) + 32 * q4;
-        if (t0 < args.T && !args.skip_out) {
+        if (t0 < args.T && !kGrad) {
           for (int a = 0; a < 2; ++a)
             tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
           bulk_commit_group();
           bulk_wait_group_read<0>();
         }
         mbar_arrive(&bars[kEmptyQ0 + st]);  // the Q tile may be refilled
+        if (kStageInV) mbar_arrive(&bars[kEmpty0 + st]);  // ... and the V tile
       }
       __syncwarp();
     }
@@ -1148,13 +1240,13 @@ size_t scan_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
 
 template <int MODE>
 static cudaError_t launch_main(const CUtensorMap& mQ, const CUtensorMap& mK, const CUtensorMap& mV,
-                               const CUtensorMap& mO, const ScanArgs& a, int64_t ctas,
-                               cudaStream_t stream) {
+                               const CUtensorMap& mO, const CUtensorMap& mR, const ScanArgs& a,
+                               int64_t ctas, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(scan_sm100_kernel<MODE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  scan_sm100_kernel<MODE><<<(unsigned)ctas, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, a);
+  scan_sm100_kernel<MODE><<<(unsigned)ctas, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, mR, a);
   return cudaGetLastError();
 }
 
@@ -1163,20 +1255,29 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
                                     unsigned flags, const ScanBackwardArgs* m, void* workspace,
                                     size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
                                     bool* encoded, int64_t in_row_elems) {
-  const int mode = m != nullptr ? m->mode : kScanNormal;
-  if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr)) {
+  int mode = m != nullptr ? m->mode : kScanNormal;
+  if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr) ||
+      (mode == kScanNormal && m != nullptr && m->grad_rows != nullptr && m->dden_out == nullptr) ||
+      ((mode == kScanRowAdd || mode == kScanRevCol) && (m->vec == nullptr || m->add == nullptr))) {
     *encoded = true;
     return cudaErrorInvalidValue;
   }
-  CUtensorMap mQ, mK, mV, mO;
+  if (mode == kScanNormal && m != nullptr && m->grad_rows != nullptr) mode = kScanNormalGrad;
+  // The epilogue's row tensor: the output gradient (no output rows are
+  // stored then) or the dot rows of mode 3.
+  const void* rows = mode == kScanNormalGrad ? m->grad_rows
+                     : (mode == kScanRevCol && m->dot_out != nullptr ? m->dot_rows : nullptr);
+  if (mode == kScanNormalGrad) out = const_cast<void*>(rows);
+  CUtensorMap mQ, mK, mV, mO, mR;
   const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems) &&
                   make_map_bthd(&mK, k, B, T, H, C, in_row_elems) &&
                   make_map_bthd(&mV, v, B, T, H, C, in_row_elems) &&
-                  make_map_bthd(&mO, out, B, T, H, 32);
+                  make_map_bthd(&mO, out, B, T, H, 32) &&
+                  make_map_bthd(&mR, rows != nullptr ? rows : out, B, T, H, 32);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   const int64_t nchunks = (T + C - 1) / C;
-  int G = mode == kScanNormal ? scan_sm100_segments(B, T, H, sms) : 1;
+  int G = (mode == kScanNormal || mode == kScanNormalGrad) ? scan_sm100_segments(B, T, H, sms) : 1;
   const size_t need = scan_sm100_workspace_bytes(B, T, H, sms);
   // Without room for the segment records the scan runs one CTA per sequence.
   if (G > 1 && (workspace == nullptr || workspace_bytes < need ||
@@ -1227,13 +1328,13 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   a.grad_rows = m ? static_cast<const __nv_bfloat16*>(m->grad_rows) : nullptr;
   a.mvec = m ? m->mvec : nullptr;
   a.dden_out = m ? m->dden_out : nullptr;
-  a.skip_out = m ? m->skip_out : 0;
   const int64_t ctas = B * H * G;
   switch (mode) {
-    case kScanRowAdd: return launch_main<kScanRowAdd>(mQ, mK, mV, mO, a, ctas, stream);
-    case kScanRevRaw: return launch_main<kScanRevRaw>(mQ, mK, mV, mO, a, ctas, stream);
-    case kScanRevCol: return launch_main<kScanRevCol>(mQ, mK, mV, mO, a, ctas, stream);
-    default: return launch_main<kScanNormal>(mQ, mK, mV, mO, a, ctas, stream);
+    case kScanRowAdd: return launch_main<kScanRowAdd>(mQ, mK, mV, mO, mR, a, ctas, stream);
+    case kScanRevRaw: return launch_main<kScanRevRaw>(mQ, mK, mV, mO, mR, a, ctas, stream);
+    case kScanRevCol: return launch_main<kScanRevCol>(mQ, mK, mV, mO, mR, a, ctas, stream);
+    case kScanNormalGrad: return launch_main<kScanNormalGrad>(mQ, mK, mV, mO, mR, a, ctas, stream);
+    default: return launch_main<kScanNormal>(mQ, mK, mV, mO, mR, a, ctas, stream);
   }
 }
 

@@ -81,6 +81,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 }
 
 // ----------------------------------------------------------------- TMA
+// Hints that pull a global line into L1 / L2 ahead of its use.
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -179,6 +187,21 @@ __device__ __forceinline__ void bulk_wait_group() {
 // (TMA stores, tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier over nthreads threads that also ORs a predicate across them:
+// every participant gets true if any passed a true `cond`.
+__device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t nthreads, bool cond) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(res)
+      : "r"((uint32_t)cond), "r"(id), "r"(nthreads)
+      : "memory");
+  return res != 0;
 }
 
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
