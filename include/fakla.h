@@ -143,7 +143,9 @@ int fakla_phi(const void* x, const void* W, const void* bias, const void* temp,
  *   dq, dk   : (B, T, H, Df) written   dv : (B, T, H, Dv) written
  *   dtemp    : (B, T, H) written, or NULL     dS0, dz0 : written, or NULL
  * Gradients have the activation dtype; all accumulation is fp32. Needs a
- * workspace of fakla_attention_backward_workspace_bytes().
+ * workspace of fakla_attention_backward_workspace_bytes() (16-byte aligned for
+ * the bf16 Df = Dv = 128 tensor-core path; with less, or unaligned tensors, the
+ * call takes the CUDA-core path).
  */
 int fakla_attention_backward(const void* q_mapped, const void* k_mapped, const void* v,
                              const void* temp, const void* dout, const float* S0,
