@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """FA-KLA prefill benchmark (one JSON line on rank 0).
 
-Workload per GPU (the reference's config 2): FA-KLA prefill, bf16 activations,
+Workload per GPU: FA-KLA prefill at B=8, H=16, T=4096, D=M=128, bf16 activations,
 fp32 state, causal, B=8, H=16, T=4096, Dk=Dv=M=128, feature map
 LearnablePositiveMap(2048 -> 2048) fused (phi(q), phi(k), then the chunked
 scan); synthetic q, k, v ~ N(0,1)/sqrt(128) from a seed, map parameters
@@ -16,7 +16,7 @@ ranks. `value` is all ranks' tokens / that time.
 
 Also reported: `e2e` (the same metric through the public API with pinned host
 buffers, host<->device copies inside the timed region), per-kernel times and
-the roofline of the dominant kernel, the recurrent decode step (config 4) in
+the roofline of the dominant kernel, the recurrent decode step (batch 256, H=32, D=128) in
 tokens/s and HBM GB/s, the CPU baseline (the reference's own CPU kernel,
 compiled from its sources into oracle/_ref, timed on a bounded sample on this
 host), SM clocks sampled through NVML during the timed region.
@@ -47,7 +47,7 @@ METRIC = "FA-KLA prefill tokens/s"
 UNIT = "tokens/s"
 # DRAM bytes (read + write) per launch from one ncu capture of each kernel on
 # these shapes (dram__bytes_read.sum + dram__bytes_write.sum), committed in
-# profiles/phi_gemm_sm100_cfg2.md and profiles/scan_sm100_cfg2.md.
+# profiles/phi_gemm_sm100_b8h16t4096.md and profiles/scan_sm100_b8h16t4096.md.
 PROFILED_DRAM_BYTES = {"phi_gemm_sm100": 276.9e6 + 233.4e6, "scan_sm100": 402.7e6 + 109.2e6}
 
 
@@ -238,10 +238,10 @@ def workload_config(world):
 # ----------------------------------------------------------------------------- single kernel
 def run_only(args):
     """One kernel of the path alone, on the benchmark's shapes: `phi` = the
-    phi GEMM for q and k of config 2 (2*65536 rows), `scan` = the chunk scan of
-    config 2 on precomputed phi, `decode` = the decode state kernel of config 4,
-    `backward` = the attention backward (temperature included) on config 2's
-    mapped shapes. Prints the mean device time per launch."""
+    phi GEMM for q and k of the B=8, H=16, T=4096 prefill (2*65536 rows), `scan` =
+    the chunk scan of that prefill on precomputed phi, `decode` = the decode state
+    kernel (batch 256, H=32), `backward` = the attention backward (temperature
+    included) on the prefill's mapped shapes. Prints the mean device time per launch."""
     from pulsartecture_b200 import _lib
 
     dev = torch.device("cuda", 0)
@@ -310,7 +310,7 @@ def run_only(args):
 
 
 def run_sustained(args):
-    """phi, scan and the phi+scan step of config 2, each launched back to back
+    """phi, scan and the phi+scan step of the B=8, H=16, T=4096 prefill, each launched back to back
     for about 1.5 s while NVML samples SM clock, power and throttle reasons
     every 5 ms (middle half of each run reported): how the kernels behave once
     the part sits at its power cap, next to the burst numbers of the main line."""
@@ -509,7 +509,7 @@ def main():
                       "copies overlapped with compute per sequence)"}
         del hq, hk, hv, hout
 
-    # ---- decode (config 4): batch 256, H=32, D=M=128, fp32 state, 1024 steps
+    # ---- decode: batch 256, H=32, D=M=128, fp32 state, 1024 steps
     decode = None
     if not args.no_decode:
         del ws
@@ -624,7 +624,7 @@ def main():
                          "achieved": phi_tflops, "peak": tflops_burst, "unit": "TFLOP/s",
                          "frac": phi_tflops / tflops_burst, "traffic": PROFILED_DRAM_BYTES["phi_gemm_sm100"],
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                           "(profiles/phi_gemm_sm100_cfg2.md)",
+                                           "(profiles/phi_gemm_sm100_b8h16t4096.md)",
                          "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS"},
             "kernels": {
                 "phi_gemm_sm100": {"ms": phi_ms, "flops": phi_flops, "tflops": phi_tflops,

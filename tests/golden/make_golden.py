@@ -119,7 +119,7 @@ def main(ref_root: str) -> None:
     LPM, TMLKA = load_reference(ref_root, ref)
     out = {}
 
-    # -- cfg1: B=2, H=4, T=256, Dk=Dv=M=64, fp32; LearnablePositiveMap(256, 256) from seed 0
+    # -- small fp32 case: B=2, H=4, T=256, Dk=Dv=M=64, fp32; LearnablePositiveMap(256, 256) from seed 0
     B, T, H, D = 2, 256, 4, 64
     torch.manual_seed(0)
     lpm = LPM(H * D, H * D)
@@ -133,12 +133,12 @@ def main(ref_root: str) -> None:
     o_ref = ref.fa_kla_attention_cpu(pq, pk, v.contiguous(), temp)
     o64, S64, z64 = O.prefill(q.numpy(), k.numpy(), v.numpy(), W.numpy(), bvec.numpy())
     assert O.rel_l2(o_ref.numpy(), o64) < 1e-5, "oracle restatement disagrees with the reference"
-    out["cfg1_W_checksum"] = checksum(W)
-    out["cfg1_b_checksum"] = checksum(bvec)
-    out["cfg1_phi_q_checksum"] = checksum(pq)
-    out["cfg1_out"] = o_ref.numpy().astype(np.float32)
-    out["cfg1_S"] = S64.astype(np.float32)
-    out["cfg1_z"] = z64.astype(np.float32)
+    out["small_W_checksum"] = checksum(W)
+    out["small_b_checksum"] = checksum(bvec)
+    out["small_phi_q_checksum"] = checksum(pq)
+    out["small_out"] = o_ref.numpy().astype(np.float32)
+    out["small_S"] = S64.astype(np.float32)
+    out["small_z"] = z64.astype(np.float32)
 
     # -- small ragged case with a temperature: B=1, H=3, T=37, Df=16, Dv=24
     q = gen((1, 37, 3, 16), 201, "uniform", 0.1, 1.5)

@@ -18,7 +18,7 @@ def gen(shape, seed):
     return torch.randn(*shape, generator=g)
 
 
-def test_prefill_f32_cfg1_matches_reference_golden(cuda):
+def test_prefill_f32_small_matches_reference_golden(cuda):
     """Config 1: B=2, H=4, T=256, Dk=Dv=M=64, fp32; LearnablePositiveMap(256,256)
     from seed 0; output and final state S, z against the reference."""
     from pulsartecture_b200.attention import fa_kla
@@ -30,9 +30,9 @@ def test_prefill_f32_cfg1_matches_reference_golden(cuda):
     m = LearnablePositiveMap(H * D, H * D).to(cuda)
     q, k, v = gen((B, T, H, D), 101), gen((B, T, H, D), 102), gen((B, T, H, D), 103)
     out, (S, z) = fa_kla(q.to(cuda), k.to(cuda), v.to(cuda), phi_weight=m.weight.detach(), phi_bias=m.bias.detach())
-    assert rel_l2(to_np(out), gold["cfg1_out"]) < F32_REL_L2
-    assert rel_l2(to_np(S), gold["cfg1_S"]) < F32_REL_L2
-    assert rel_l2(to_np(z), gold["cfg1_z"]) < F32_REL_L2
+    assert rel_l2(to_np(out), gold["small_out"]) < F32_REL_L2
+    assert rel_l2(to_np(S), gold["small_S"]) < F32_REL_L2
+    assert rel_l2(to_np(z), gold["small_z"]) < F32_REL_L2
 
 
 def test_module_f32_matches_reference_module_golden(cuda):
@@ -96,7 +96,7 @@ def test_prefill_state_handoff_is_exact(cuda):
     assert torch.equal(S2, S) and torch.equal(z2, z)
 
 
-def test_prefill_bf16_cfg2_full_size(cuda):
+def test_prefill_bf16_b8h16t4096_full_size(cuda):
     """Config 2 at full size (B=8, H=16, T=4096, D=M=128, bf16): oracle on three
     (b, h) sequences, size-independent checks on all of them."""
     from pulsartecture_b200.attention import fa_kla

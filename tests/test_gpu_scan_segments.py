@@ -91,7 +91,7 @@ def test_segmented_matches_oracle_and_single_cta(cuda, B, T, H, with_temp, with_
     assert rel_l2(to_np(out_a), to_np(out_b)) < 2e-3
 
 
-def test_long_context_cfg3_full_size(cuda):
+def test_long_context_b1h32t65536_full_size(cuda):
     """Long-context prefill at full size: B=1, H=32, T=65536, Dk=Dv=M=128,
     bf16, LearnablePositiveMap(4096 -> 4096) from seed 0. The scan is checked
     against the oracle on two whole sequences (fed the kernel's own phi, which

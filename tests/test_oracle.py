@@ -40,11 +40,11 @@ def test_lpm_init_matches_reference_checksums(golden):
 
     torch.manual_seed(0)
     m = LearnablePositiveMap(256, 256)
-    np.testing.assert_allclose(checksum(m.weight.detach()), golden["cfg1_W_checksum"], rtol=1e-12)
-    np.testing.assert_allclose(checksum(m.bias.detach()), golden["cfg1_b_checksum"], rtol=1e-12)
+    np.testing.assert_allclose(checksum(m.weight.detach()), golden["small_W_checksum"], rtol=1e-12)
+    np.testing.assert_allclose(checksum(m.bias.detach()), golden["small_b_checksum"], rtol=1e-12)
 
 
-def test_oracle_cfg1_against_golden(golden):
+def test_oracle_small_against_golden(golden):
     B, T, H, D = 2, 256, 4, 64
     torch.manual_seed(0)
     from pulsartecture_b200.kernels.feature_maps import LearnablePositiveMap
@@ -53,11 +53,11 @@ def test_oracle_cfg1_against_golden(golden):
     W, b = m.weight.detach().numpy(), m.bias.detach().numpy()
     q, k, v = gen((B, T, H, D), 101), gen((B, T, H, D), 102), gen((B, T, H, D), 103)
     out, S, z = O.prefill(q.numpy(), k.numpy(), v.numpy(), W, b)
-    assert rel_l2(out, golden["cfg1_out"]) < 1e-6
-    assert rel_l2(S, golden["cfg1_S"]) < 1e-6
-    assert rel_l2(z, golden["cfg1_z"]) < 1e-6
+    assert rel_l2(out, golden["small_out"]) < 1e-6
+    assert rel_l2(S, golden["small_S"]) < 1e-6
+    assert rel_l2(z, golden["small_z"]) < 1e-6
     pq = O.phi(q.numpy().reshape(B, T, H * D), W, b)
-    np.testing.assert_allclose(checksum(torch.from_numpy(pq)), golden["cfg1_phi_q_checksum"], rtol=1e-6)
+    np.testing.assert_allclose(checksum(torch.from_numpy(pq)), golden["small_phi_q_checksum"], rtol=1e-6)
 
 
 def test_oracle_ragged_temp_against_golden(golden):
