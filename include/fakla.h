@@ -286,7 +286,7 @@ size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim,
  *   bias : (2*H*M + H*Dv) = [Wphi bq + bphi ; Wphi bk + bphi ; bv], or NULL
  *   temp : (B, T, H) or NULL     out : (B, T, H, Dv)
  *   S, z, flags : as fakla_attention, with Df = M.
- * Implemented for BF16 with M = Dv = 128, embed % 64 == 0, (2*H*M + H*Dv) %
+ * Implemented for BF16 with M = Dv = 128 or 64, embed % 64 == 0, (2*H*M + H*Dv) %
  * 256 == 0, 16-byte aligned pointers; other cases return FAKLA_ERR_UNSUPPORTED.
  * Workspace: fakla_qkv_prefill_workspace_bytes() (the GEMM output, then the
  * scan's optional segment records).

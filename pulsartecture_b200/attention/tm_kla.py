@@ -151,7 +151,7 @@ class TMLinKernelAttn(nn.Module):
             return False
         dt = mapper.weight.dtype
         H, M, Dv = self.num_heads, self.feature_dim // self.num_heads, self.v_head_dim
-        return (x.is_cuda and dt == torch.bfloat16 and M == 128 and Dv == 128 and self.embed_dim % 64 == 0
+        return (x.is_cuda and dt == torch.bfloat16 and M == Dv and M in (64, 128) and self.embed_dim % 64 == 0
                 and (2 * H * M + H * Dv) % 256 == 0 and self.feature_dim % self.num_heads == 0)
 
     def _qkv_fold(self):

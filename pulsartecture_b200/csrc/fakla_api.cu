@@ -216,7 +216,7 @@ int run_attention(const void* q, const void* k, const void* v, const void* temp,
   if (use_sm100_scan(dtype, q, k, v, out, S, B, T, H, Df, Dv)) {
     bool enc = false;
     cudaError_t e = fakla::launch_scan_sm100(q, k, v, temp, out, S, z, B, T, H, flags, workspace,
-                                             workspace_bytes, d->sms, stream, d->status, &enc);
+                                             workspace_bytes, d->sms, stream, d->status, &enc, 0, Df);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
     return FAKLA_OK;
@@ -524,12 +524,12 @@ extern "C" int fakla_qkv_prefill(const void* x, const void* W, const void* bias,
     return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
   if ((rc = check_state(S, z, flags))) return rc;
   const int64_t rows = B * T;
-  if (dtype != FAKLA_BF16 || M != 128 || Dv != 128 ||
+  if (dtype != FAKLA_BF16 || M != Dv || (M != 128 && M != 64) ||
       !fakla::qkv_sm100_supported(rows, embed, H * M, H * Dv, H) ||
       !fakla::scan_sm100_supported(B, T, H, M, Dv))
     return fakla_set_error(FAKLA_ERR_UNSUPPORTED,
-                           "fakla_qkv_prefill serves bf16, M = Dv = 128, embed %% 64 == 0 (got dtype=%d M=%lld "
-                           "Dv=%lld embed=%lld)", dtype, (long long)M, (long long)Dv, (long long)embed);
+                           "fakla_qkv_prefill serves bf16, M = Dv = 128 or 64, embed %% 64 == 0 (got dtype=%d "
+                           "M=%lld Dv=%lld embed=%lld)", dtype, (long long)M, (long long)Dv, (long long)embed);
   if (!aligned16(x) || !aligned16(W) || !aligned16(out) || (bias && !aligned16(bias)) ||
       (S && !aligned16(S)))
     return fakla_set_error(FAKLA_ERR_ALIGNMENT, "x, W, bias, out and S must be 16-byte aligned");
@@ -553,7 +553,7 @@ extern "C" int fakla_qkv_prefill(const void* x, const void* W, const void* bias,
   const void* phk = buf + (size_t)H * M * 2;
   const void* vv = buf + (size_t)2 * H * M * 2;
   e = fakla::launch_scan_sm100(phq, phk, vv, nullptr, out, S, z, B, T, H, flags, buf + need,
-                               workspace_bytes - need, d->sms, st, d->status, &enc, row_elems);
+                               workspace_bytes - need, d->sms, st, d->status, &enc, row_elems, M);
   if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
   if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
   return FAKLA_OK;

@@ -56,6 +56,8 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
                              const void* temp0, const void* temp1, void* out0, void* out1,
                              int64_t rows, int64_t K, int64_t N, int64_t heads, int act,
                              float scale, cudaStream_t stream, int* status, bool* encoded);
+// Df = Dv = 128, or 64 (the forward only: run in the 128-wide tiles with the
+// second half held at zero).
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
 // Segments per sequence the scan uses on a device with `sms` SMs (1 = one CTA
 // per sequence), and the workspace that takes (0 when G = 1).
@@ -67,7 +69,7 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
                               cudaStream_t stream, int* status, bool* encoded,
-                              int64_t in_row_elems = 0);
+                              int64_t in_row_elems = 0, int64_t head_dim = 128);
 
 // Tensor-core backward (sm100_backward.cu): bf16, Df = Dv = 128.
 bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);

@@ -188,7 +188,7 @@ BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
 }  // namespace
 
 bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
-  return dtype == FAKLA_BF16 && scan_sm100_supported(B, T, H, Df, Dv) &&
+  return dtype == FAKLA_BF16 && Df == D && Dv == D && scan_sm100_supported(B, T, H, Df, Dv) &&
          B * T * H <= (int64_t)INT32_MAX;
 }
 

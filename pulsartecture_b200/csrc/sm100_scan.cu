@@ -116,6 +116,8 @@ struct ScanArgs {
   int seg_chunks;             // chunks per segment
   unsigned flags;
   int* status;
+  int hd;  // head size: 128, or 64 (features and values in the first 64 columns of
+           // each tile, whose second 64-column atom stays zero; kScanNormal only)
   // backward passes (modes below)
   const __nv_bfloat16* grad_rows;  // kScanNormalGrad: (B,T,H,D) output gradient -> dden_out (no output rows)
   float* dden_out;                 // (B,T,H): -(bf16(g/den) . out) (g = grad_rows)
@@ -486,6 +488,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   // ONES: rows 4-5 of M0 (256 bytes of bf16 1.0).
   if (threadIdx.x < 64)
     reinterpret_cast<uint32_t*>(sM0 + 512)[threadIdx.x] = 0x3F803F80u;
+  // 64-wide heads: the second atom of every Q, K and V tile is zero for the
+  // whole kernel (no load writes it; the output is staged in the first atom
+  // only), so the MMAs see zero features and values past column 64.
+  const int na = args.hd == 64 ? 1 : 2;  // 64-column atoms loaded per tile
+  if (na == 1) {
+    constexpr int kPer = kAtom / 16;
+    for (int o = threadIdx.x; o < 3 * kStages * kPer; o += kThreads) {
+      const int t = o / kPer;  // Q0 Q1 K0 K1 V0 V1
+      uint8_t* base = (t < 2 ? sQ : (t < 4 ? sK : sV)) + (t & 1) * kTile + kAtom;
+      reinterpret_cast<uint4*>(base)[o % kPer] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -509,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           break;
         }
         uint64_t* fb = &bars[kFull0 + st];
-        mbar_arrive_expect_tx(fb, 3 * kTile);
+        mbar_arrive_expect_tx(fb, 3 * na * kAtom);
         const int t0 = chunk_t0(i);
         if constexpr (kRaw) {
           for (int a = 0; a < 2; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
@@ -522,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           }
           for (int a = 0; a < 2; ++a) tma_load_4d(sK + a * kAtom, &tmK, fb, a * 64, h, t0, b);
         } else {
-          for (int a = 0; a < 2; ++a) {
+          for (int a = 0; a < na; ++a) {
             tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
             tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
           }
@@ -535,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           *abort_flag = 1;
           break;
         }
-        for (int a = 0; a < 2; ++a)
+        for (int a = 0; a < na; ++a)
           tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, t0, b);
       }
       if (*abort_flag) {
@@ -698,23 +712,26 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       // or transposed: column r), else 0
       const float* srow = nullptr;
       const float* scol = nullptr;
+      int srow_len = D;  // columns of srow (the caller's S of a 64-wide head has 64)
       float z0 = 0.f;
       if (args.seg_init != nullptr) {
         const float* rec = args.seg_init + (bh * args.G + seg) * kStateFloats;
         srow = rec + (int64_t)r * D;
         z0 = rec[(int64_t)D * D + r];
-      } else if ((args.flags & FAKLA_STATE_IN) && args.S != nullptr) {
+      } else if ((args.flags & FAKLA_STATE_IN) && args.S != nullptr && r < args.hd) {
+        const int hd = args.hd;
         if (args.state_in_T)
           scol = args.S + bh * D * D + r;
         else
-          srow = args.S + (bh * D + r) * D;
-        if (!kRaw) z0 = args.z[bh * D + r];
+          srow = args.S + (bh * hd + r) * hd;
+        srow_len = hd;
+        if (!kRaw) z0 = args.z[bh * hd + r];
       }
 #pragma unroll 1
       for (int cc = 0; cc < D; cc += 16) {
         uint32_t v[16];
         float f[16];
-        if (srow != nullptr) {
+        if (srow != nullptr && cc < srow_len) {
           const float4* s4 = reinterpret_cast<const float4*>(srow + cc);
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -780,8 +797,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           for (int e = 0; e < 8; ++e) f8[e] = __uint_as_float(v[8 * g + e]);
           put_sb8<kRaw>(sSb, sSbLo, r, cc + 8 * g, f8);
         }
-        if (sout) {
-          float4* dst = reinterpret_cast<float4*>(args.S + (bh * D + r) * D + cc);
+        if (sout && r < args.hd && cc < args.hd) {
+          float4* dst = reinterpret_cast<float4*>(args.S + (bh * args.hd + r) * args.hd + cc);
 #pragma unroll
           for (int g = 0; g < 8; ++g)
             dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
@@ -794,7 +811,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         tmem_ld_wait();
         const float zf = __uint_as_float(zraw);
         put_zk(sM0, r, zf);
-        if (!kRaw && sout) args.z[bh * D + r] = zf;
+        if (!kRaw && sout && r < args.hd) args.z[bh * args.hd + r] = zf;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -896,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (live) args.dden_out[row] = -acc;
       } else if (!kAffine) {
 #pragma unroll 1
-        for (int cc = 0; cc < D; cc += 64) {
+        for (int cc = 0; cc < args.hd; cc += 64) {
           uint32_t va[32], vb[32];
           tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
           tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
@@ -946,7 +963,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       if (lane == 0) {
         const int t0 = chunk_t0(i) + 32 * q4;
         if (t0 < args.T && !kGrad) {
-          for (int a = 0; a < 2; ++a)
+          for (int a = 0; a < na; ++a)
             tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
           bulk_commit_group();
           bulk_wait_group_read<0>();
@@ -999,6 +1016,7 @@ struct DeltaArgs {
   float* seg_init;  // (B*H, G) records
   int T, H, G, seg_chunks;
   int* status;
+  int hd;  // 128, or 64 (second atom of each tile held at zero)
 };
 
 __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
@@ -1040,6 +1058,15 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
     tma_prefetch_desc(&tmV);
   }
   if (threadIdx.x < 64) reinterpret_cast<uint32_t*>(sOnes)[threadIdx.x] = 0x3F803F80u;
+  const int na = args.hd == 64 ? 1 : 2;  // 64-column atoms loaded per tile
+  if (na == 1) {
+    constexpr int kPer = kAtom / 16;
+    for (int o = threadIdx.x; o < 2 * kDStages * kPer; o += kDThreads) {
+      const int t = o / kPer;  // K and V tile of each stage
+      uint8_t* base = sSt + (t >> 1) * kDTile + (t & 1) * kTile + kAtom;
+      reinterpret_cast<uint4*>(base)[o % kPer] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 256);
@@ -1063,10 +1090,10 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
           break;
         }
         uint64_t* fb = &bars[kDFull0 + st];
-        mbar_arrive_expect_tx(fb, 2 * kTile);
+        mbar_arrive_expect_tx(fb, 2 * na * kAtom);
         const int t0 = (c0 + i) * C;
         uint8_t* tk = sSt + st * kDTile;
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < na; ++a) {
           tma_load_4d(tk + a * kAtom, &tmK, fb, a * 64, h, t0, b);
           tma_load_4d(tk + kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
         }
@@ -1170,7 +1197,7 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
 // record g-1 + the segment sum stored in record g. One thread per float4 of
 // a record, sequential over the G records (coalesced across threads).
 __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const float* z_in, int G,
-                                   int state_in) {
+                                   int state_in, int hd) {
   constexpr int kS4 = D * D / 4;
   constexpr int kRec4 = (int)(kStateFloats / 4);
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1179,11 +1206,17 @@ __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const flo
   float4* rec = reinterpret_cast<float4*>(seg_init + bh * G * kStateFloats);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (state_in) {
+    // the caller's state is hd x hd (+ hd); records are D x D (+ D), zero-padded
     if (i < kS4) {
-      acc = reinterpret_cast<const float4*>(S_in + bh * D * D)[i];
+      const int f = (4 * i) / D, d = (4 * i) % D;
+      if (f < hd && d < hd)
+        acc = *reinterpret_cast<const float4*>(S_in + (bh * hd + f) * hd + d);
     } else {
-      const float* zp = z_in + bh * D + 4 * (i - kS4);
-      acc = make_float4(zp[0], zp[1], zp[2], zp[3]);
+      const int f = 4 * (i - kS4);
+      if (f < hd) {
+        const float* zp = z_in + bh * hd + f;
+        acc = make_float4(zp[0], zp[1], zp[2], zp[3]);
+      }
     }
   }
   rec[i] = acc;
@@ -1203,13 +1236,13 @@ __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const flo
 // Host side
 // ---------------------------------------------------------------------------
 static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t H,
-                          int box_t = C, int64_t row_elems = 0) {
-  // (B, T, H, 128) bf16 viewed as 4-D {d, h, t, b}; box = 64 d x 1 h x box_t t x 1 b.
-  // row_elems: elements from one token's row to the next (H * 128 when dense;
+                          int box_t = C, int64_t row_elems = 0, int64_t hd = D) {
+  // (B, T, H, hd) bf16 viewed as 4-D {d, h, t, b}; box = 64 d x 1 h x box_t t x 1 b.
+  // row_elems: elements from one token's row to the next (H * hd when dense;
   // larger for a column block of a wider row, e.g. the q/k/v GEMM output).
-  const int64_t re = row_elems > 0 ? row_elems : H * D;
-  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)re * 2, (cuuint64_t)T * re * 2};
+  const int64_t re = row_elems > 0 ? row_elems : H * hd;
+  const cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)re * 2, (cuuint64_t)T * re * 2};
   const cuuint32_t box[4] = {64, 1, (cuuint32_t)box_t, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
@@ -1217,8 +1250,8 @@ static bool make_map_bthd(CUtensorMap* map, const void* base, int64_t B, int64_t
 }
 
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
-  return Df == D && Dv == D && B >= 1 && T >= 1 && H >= 1 && B * H <= (int64_t)(INT32_MAX / 256) &&
-         T <= (int64_t)INT32_MAX - C;
+  return Df == Dv && (Df == D || Df == 64) && B >= 1 && T >= 1 && H >= 1 &&
+         B * H <= (int64_t)(INT32_MAX / 256) && T <= (int64_t)INT32_MAX - C;
 }
 
 int scan_sm100_segments(int64_t B, int64_t T, int64_t H, int sms) {
@@ -1254,9 +1287,10 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
                                     void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                                     unsigned flags, const ScanBackwardArgs* m, void* workspace,
                                     size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
-                                    bool* encoded, int64_t in_row_elems) {
+                                    bool* encoded, int64_t in_row_elems, int64_t hd) {
   int mode = m != nullptr ? m->mode : kScanNormal;
   if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr) ||
+      (hd != D && (hd != 64 || m != nullptr)) ||
       (mode == kScanNormal && m != nullptr && m->grad_rows != nullptr && m->dden_out == nullptr) ||
       ((mode == kScanRowAdd || mode == kScanRevCol) && (m->vec == nullptr || m->add == nullptr))) {
     *encoded = true;
@@ -1269,11 +1303,11 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
                      : (mode == kScanRevCol && m->dot_out != nullptr ? m->dot_rows : nullptr);
   if (mode == kScanNormalGrad) out = const_cast<void*>(rows);
   CUtensorMap mQ, mK, mV, mO, mR;
-  const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems) &&
-                  make_map_bthd(&mK, k, B, T, H, C, in_row_elems) &&
-                  make_map_bthd(&mV, v, B, T, H, C, in_row_elems) &&
-                  make_map_bthd(&mO, out, B, T, H, 32) &&
-                  make_map_bthd(&mR, rows != nullptr ? rows : out, B, T, H, 32);
+  const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems, hd) &&
+                  make_map_bthd(&mK, k, B, T, H, C, in_row_elems, hd) &&
+                  make_map_bthd(&mV, v, B, T, H, C, in_row_elems, hd) &&
+                  make_map_bthd(&mO, out, B, T, H, 32, 0, hd) &&
+                  make_map_bthd(&mR, rows != nullptr ? rows : out, B, T, H, 32, 0, hd);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   const int64_t nchunks = (T + C - 1) / C;
@@ -1295,6 +1329,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
     d.H = (int)H;
     d.G = G;
     d.seg_chunks = seg_chunks;
+    d.hd = (int)hd;
     d.status = status;
     cudaError_t e = cudaFuncSetAttribute(scan_delta_sm100_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1303,7 +1338,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
     scan_delta_sm100_kernel<<<(unsigned)(B * H * (G - 1)), kDThreads, kDSmemBytes, stream>>>(mK, mV, d);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const dim3 pgrid((unsigned)((kStateFloats / 4 + 255) / 256), (unsigned)(B * H));
-    scan_prefix_kernel<<<pgrid, 256, 0, stream>>>(seg_init, S, z, G, state_in ? 1 : 0);
+    scan_prefix_kernel<<<pgrid, 256, 0, stream>>>(seg_init, S, z, G, state_in ? 1 : 0, (int)hd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
 
@@ -1318,6 +1353,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   a.seg_chunks = seg_chunks;
   a.flags = flags;
   a.status = status;
+  a.hd = (int)hd;
   a.add = m ? m->add : nullptr;
   a.den_out = m ? m->den_out : nullptr;
   a.state_in_T = m ? m->state_in_T : 0;
@@ -1341,9 +1377,10 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
 cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const void* temp,
                               void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                               unsigned flags, void* workspace, size_t workspace_bytes, int sms,
-                              cudaStream_t stream, int* status, bool* encoded, int64_t in_row_elems) {
+                              cudaStream_t stream, int* status, bool* encoded, int64_t in_row_elems,
+                              int64_t hd) {
   return launch_scan_impl(q, k, v, temp, out, S, z, B, T, H, flags, nullptr, workspace,
-                          workspace_bytes, sms, stream, status, encoded, in_row_elems);
+                          workspace_bytes, sms, stream, status, encoded, in_row_elems, hd);
 }
 
 cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, const void* temp,
@@ -1352,7 +1389,7 @@ cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, 
                                    size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
                                    bool* encoded) {
   return launch_scan_impl(q, k, v, temp, out, S, z, B, T, H, flags, &m, workspace, workspace_bytes,
-                          sms, stream, status, encoded, 0);
+                          sms, stream, status, encoded, 0, D);
 }
 
 }  // namespace fakla

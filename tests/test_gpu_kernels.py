@@ -105,11 +105,13 @@ ATT_BF16_CASES = [
 ]
 
 
-@pytest.mark.parametrize("B,T,H,with_temp,with_state", ATT_BF16_CASES)
-def test_attention_bf16_tensor_core(cuda, B, T, H, with_temp, with_state):
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("B,T,H,with_temp,with_state", ATT_BF16_CASES + [(1, 3000, 2, True, True)])
+def test_attention_bf16_tensor_core(cuda, B, T, H, with_temp, with_state, D):
+    """Heads of 128, and of 64 (run in the 128-wide tiles with the second half
+    held at zero); the long few-sequence cases take the segmented scan."""
     from pulsartecture_b200.backend.interface import fa_kla_attention_with_state
 
-    D = 128
     q = _phi_like((B, T, H, D), 10, cuda, torch.bfloat16)
     k = _phi_like((B, T, H, D), 11, cuda, torch.bfloat16)
     v = _normal((B, T, H, D), 12, cuda, torch.bfloat16, 1 / np.sqrt(D))

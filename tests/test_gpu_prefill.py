@@ -204,17 +204,19 @@ def test_prefill_host_rejects_device_inputs(cuda):
         fa_kla_host(x, x, torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16), phi_weight=W)
 
 
-@pytest.mark.parametrize("T,with_temp", [(300, True), (1024, False)])
-def test_module_qkv_folded_into_phi(cuda, T, with_temp):
+@pytest.mark.parametrize("T,with_temp,H,D", [(300, True, 4, 128), (1024, False, 4, 128),
+                                               (300, True, 8, 64), (777, False, 16, 64)])
+def test_module_qkv_folded_into_phi(cuda, T, with_temp, H, D):
     """Inference through fakla_qkv_prefill (projections folded into the feature
     map, one GEMM for [phi(q) | phi(k) temp | v]): equal to the projections,
     map and attention of the reference restated in float64 on the same bf16
-    parameters, within the bf16 bars; the returned state too."""
+    parameters, within the bf16 bars; the returned state too. Heads of 128 and
+    of 64."""
     from pulsartecture_b200.attention import TMLinKernelAttn
     from pulsartecture_b200.kernels import LearnablePositiveMap
 
     torch.manual_seed(7)
-    E, H, D = 512, 4, 128
+    E = 512 if H * D == 512 else H * D
     mapper = LearnablePositiveMap(H * D, H * D, dtype=torch.bfloat16)
     mod = TMLinKernelAttn(E, mapper, num_heads=H, qk_dim=D, v_dim=D, temp_input_dim=16 if with_temp else 0,
                           dtype=torch.bfloat16).to(cuda).eval()

@@ -51,9 +51,11 @@ def test_workspace_query_segments_only_when_sms_would_idle(cuda):
     # 32 long sequences: 4 segments each, one (S, z) record per segment
     rec = (128 * 128 + 128) * 4
     assert L.fakla_attention_workspace_bytes(1, 65536, 32, 128, 128, bf) == 32 * 4 * rec
+    # 64-wide heads run in the same tiles: the same records
+    assert L.fakla_attention_workspace_bytes(1, 65536, 32, 64, 64, bf) == 32 * 4 * rec
     # fp32 and other head dims run on the CUDA-core scan: no workspace
     assert L.fakla_attention_workspace_bytes(1, 65536, 32, 128, 128, _lib.FAKLA_F32) == 0
-    assert L.fakla_attention_workspace_bytes(1, 65536, 2, 64, 64, bf) == 0
+    assert L.fakla_attention_workspace_bytes(1, 65536, 2, 32, 32, bf) == 0
 
 
 @pytest.mark.parametrize("B,T,H,with_temp,with_state", [
