@@ -379,6 +379,65 @@ def run_sustained(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- LM harness
+def run_lm(args):
+    """Forward of the package's own end-to-end LM composition (lm_harness.py:
+    the reference ships no model) at 12 layers, d_model 1024, 16 FA-KLA heads
+    of 64, top-2 of 8 experts with d_ff 4096, vocabulary 32000, B=16, T=2048,
+    bf16, random weights from seed 0 and uniform token ids. Prints tokens/s
+    and the share of the time spent in the FA-KLA sublayers (CUDA events
+    around each TMLinKernelAttn call on the launching stream)."""
+    from pulsartecture_b200.lm_harness import FaklaLM
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B_, T_ = 16, 2048
+    torch.manual_seed(0)
+    model = FaklaLM(dtype=torch.bfloat16, device=dev).eval()
+    g = torch.Generator(device=dev).manual_seed(1)
+    ids = torch.randint(0, 32000, (B_, T_), generator=g, device=dev)
+    marks = []
+
+    def pre(mod, inp):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append(e)
+
+    def post(mod, inp, out):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append(e)
+
+    hooks = []
+    for blk in model.blocks:
+        hooks.append(blk.attn.register_forward_pre_hook(pre))
+        hooks.append(blk.attn.register_forward_hook(post))
+    with torch.no_grad():
+        assert model.blocks[0].attn._qkv_foldable(model.embed(ids))
+        for _ in range(args.warmup):
+            model(ids)
+        torch.cuda.synchronize()
+        marks.clear()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            logits = model(ids)
+        e1.record()
+        e1.synchronize()
+    for h in hooks:
+        h.remove()
+    ms = e0.elapsed_time(e1) / args.steps
+    attn_ms = sum(marks[i].elapsed_time(marks[i + 1]) for i in range(0, len(marks), 2)) / args.steps
+    line = {"only": "lm", "model": "FA-KLA LM (this package's composition; no reference model exists)",
+            "config": {"layers": 12, "d_model": 1024, "heads": 16, "head_dim": 64, "experts": "top-2 of 8",
+                       "d_ff": 4096, "vocab": 32000, "batch": B_, "seq_len": T_, "dtype": "bf16"},
+            "ms_per_forward": round(ms, 3), "tokens_per_s": round(B_ * T_ / ms * 1e3, 1),
+            "fakla_ms_per_forward": round(attn_ms, 3), "fakla_share": round(attn_ms / ms, 4),
+            "logits_finite": bool(torch.isfinite(logits.float()).all().item())}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -391,7 +450,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-module", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained"],
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -399,6 +458,8 @@ def main():
         return run_reference_arm(args)
     if args.only == "sustained":
         return run_sustained(args)
+    if args.only == "lm":
+        return run_lm(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
