@@ -221,14 +221,18 @@ __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
 // The kept values first get `arow` (a per-row term) and bcol[s - sbase] (a
 // per-column term: 32 floats in shared memory, the same for every row).
 // Returns the sum of the kept values.
-template <int kMask, bool kCol>
+template <int kMask, bool kCol, bool kRow>
 __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase, int r,
                                              uint32_t p_addr, float arow, const float* bcol) {
   uint32_t hi[16], lo[16];
   float rs = 0.f;
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    float x0 = __uint_as_float(v[2 * e]) + arow, x1 = __uint_as_float(v[2 * e + 1]) + arow;
+    float x0 = __uint_as_float(v[2 * e]), x1 = __uint_as_float(v[2 * e + 1]);
+    if (kRow) {  // (x + 0 is not folded away: keep the add out of the other modes)
+      x0 += arow;
+      x1 += arow;
+    }
     if (kCol) {
       const float2 bb = reinterpret_cast<const float2*>(bcol)[e];
       x0 += bb.x;
@@ -256,11 +260,11 @@ __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase,
 // Row r of P, token group g (32 tokens) of a warp whose rows are the group
 // q4. Causal: groups below the diagonal are kept whole, the diagonal one is
 // masked. Reversed: groups above the diagonal are kept whole.
-template <bool kRev, bool kCol>
+template <bool kRev, bool kCol, bool kRow>
 __device__ __forceinline__ float split_group_at(const uint32_t (&v)[32], int g, int q4, int r,
                                                 uint32_t p_addr, float arow, const float* bcol) {
-  return g == q4 ? split_group<kRev ? 2 : 1, kCol>(v, 32 * g, r, p_addr, arow, bcol)
-                 : split_group<0, kCol>(v, 32 * g, r, p_addr, arow, bcol);
+  return g == q4 ? split_group<kRev ? 2 : 1, kCol, kRow>(v, 32 * g, r, p_addr, arow, bcol)
+                 : split_group<0, kCol, kRow>(v, 32 * g, r, p_addr, arow, bcol);
 }
 
 // Outside the kept triangle the whole group is masked: hi = lo = 0.
@@ -683,11 +687,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (k1) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
         tmem_ld_wait();
         if (k0)
-          rs += split_group_at<kRev, kCol>(va, g0, q4, r, p_addr, arow, bcol_sm + 32 * g0);
+          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd>(va, g0, q4, r, p_addr, arow, bcol_sm + 32 * g0);
         else
           zero_group(g0, p_addr);
         if (k1)
-          rs += split_group_at<kRev, kCol>(vb, g0 + 1, q4, r, p_addr, arow, bcol_sm + 32 * g0 + 32);
+          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd>(vb, g0 + 1, q4, r, p_addr, arow, bcol_sm + 32 * g0 + 32);
         else
           zero_group(g0 + 1, p_addr);
       }
