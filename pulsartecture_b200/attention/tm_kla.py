@@ -264,14 +264,18 @@ def fa_kla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[St
 def fa_kla_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[State] = None, *,
                 phi_weight: torch.Tensor, phi_bias: Optional[torch.Tensor] = None,
                 temp: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                micro_batch: int = 1) -> Tuple[torch.Tensor, State]:
+                micro_batch: int = 1, ordered: bool = True) -> Tuple[torch.Tensor, State]:
     """``fa_kla`` for inputs that live in host memory: q, k, v (and temp) on the
     CPU, phi_weight/phi_bias on the GPU that runs the call; returns the output
     in host memory and the state on the GPU. Transfers in both directions
     overlap the compute of neighbouring groups of ``micro_batch`` sequences.
     The output is complete once the current CUDA stream has reached the call.
+    ordered=False lets back-to-back calls overlap their copies (the host
+    inputs must not be written by device work still pending on the current
+    stream; see fa_kla_prefill_host).
     """
-    return fa_kla_prefill_host(q, k, v, phi_weight, phi_bias, temp, state, True, out, micro_batch)
+    return fa_kla_prefill_host(q, k, v, phi_weight, phi_bias, temp, state, True, out, micro_batch,
+                               ordered=ordered)
 
 
 def fa_kla_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: State, *,

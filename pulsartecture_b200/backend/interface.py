@@ -292,10 +292,45 @@ def device_status(stream: Optional[torch.cuda.Stream] = None) -> None:
     _lib.check(_lib.lib().fakla_device_status(s.cuda_stream))
 
 
+class _HostPipeline:
+    """Side streams, device slot buffers and per-slot events of
+    fa_kla_prefill_host, kept from one call to the next of the same shape
+    (one pipeline per device): a call's input copies then only wait for the
+    slot they refill, not for the previous call's last output copy."""
+
+    def __init__(self, dev, key, mb, T, q_tail, H, Dv, dt, with_temp, ws_bytes, ns):
+        self.key = key
+        self.s_in = torch.cuda.Stream(dev)
+        self.s_out = torch.cuda.Stream(dev)
+        self.bq = [torch.empty((mb,) + q_tail, device=dev, dtype=dt) for _ in range(ns)]
+        self.bk = [torch.empty((mb,) + q_tail, device=dev, dtype=dt) for _ in range(ns)]
+        self.bv = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
+        self.bt = [torch.empty((mb, T, H), device=dev, dtype=dt) for _ in range(ns)] if with_temp else None
+        self.bo = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
+        self.bw = [torch.empty(ws_bytes, device=dev, dtype=torch.uint8) for _ in range(ns)]
+        # the buffers come from the caching allocator on the caller's stream:
+        # the side streams start after whatever last used that memory
+        born = torch.cuda.Event()
+        born.record(torch.cuda.current_stream(dev))
+        self.s_in.wait_event(born)
+        self.s_out.wait_event(born)
+        self.in_free = [None] * ns   # the prefill that last read the slot's inputs
+        self.out_free = [None] * ns  # the copy that last read the slot's output
+
+
+_HOST_PIPES: dict = {}
+
+
+def release_host_pipelines() -> None:
+    """Free the device buffers fa_kla_prefill_host keeps between calls."""
+    _HOST_PIPES.clear()
+
+
 def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
                         bias: Optional[torch.Tensor] = None, temp: Optional[torch.Tensor] = None,
                         state: Optional[State] = None, return_state: bool = True,
-                        out: Optional[torch.Tensor] = None, micro_batch: int = 1, slots: int = 3):
+                        out: Optional[torch.Tensor] = None, micro_batch: int = 1, slots: int = 3,
+                        ordered: bool = True):
     """phi fused with FA-KLA on HOST tensors, transfers overlapped with compute.
 
     q, k: (B, T, in_dim) or (B, T, H_in, Dk) on the CPU (pin them for
@@ -311,6 +346,15 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     given), state (S, z) on the GPU. Like a ``non_blocking`` copy, the call
     returns once the work is queued; ``out`` is complete when the caller's
     current stream reaches this point (e.g. after ``torch.cuda.synchronize()``).
+
+    ordered=True starts the input copies after all work queued so far on the
+    caller's stream (as a copy on that stream would). ordered=False starts
+    them as soon as their device slot is free, so back-to-back calls overlap
+    one call's last output copy with the next call's first input copies; the
+    host inputs must then not be written by device work still pending on the
+    caller's stream (host-side writes before the call are fine). The device
+    buffers are kept for the next call of the same shape
+    (release_host_pipelines() frees them).
     """
     _require(weight.is_cuda, "weight must be a CUDA tensor: it selects the GPU that runs the call")
     dev = weight.device
@@ -320,8 +364,8 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     _require(v.dim() == 4, "v must be 4D (B, T, H, Dv)")
     B, T = q.shape[0], q.shape[1]
     in_dim = 1
-    for s in q.shape[2:]:
-        in_dim *= s
+    for s_ in q.shape[2:]:
+        in_dim *= s_
     _require(tuple(v.shape[:2]) == (B, T), "B, T dimensions must match for q/k/v")
     H, Dv = v.shape[2], v.shape[3]
     _require(weight.dim() == 2 and weight.shape[1] == in_dim, f"weight must be (H*M, {in_dim})")
@@ -349,58 +393,56 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     ws_bytes = L.fakla_prefill_workspace_bytes(mb, T, in_dim, H, M, Dv, code)
     with torch.cuda.device(dev):
         main = torch.cuda.current_stream(dev)
-        s_in = torch.cuda.Stream(dev)
-        s_out = torch.cuda.Stream(dev)
-        # per slot: inputs, output, workspace (allocated on the main stream)
-        bq = [torch.empty((mb,) + tuple(q.shape[1:]), device=dev, dtype=dt) for _ in range(ns)]
-        bk = [torch.empty((mb,) + tuple(q.shape[1:]), device=dev, dtype=dt) for _ in range(ns)]
-        bv = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
-        bt = [torch.empty((mb, T, H), device=dev, dtype=dt) for _ in range(ns)] if temp is not None else None
-        bo = [torch.empty((mb, T, H, Dv), device=dev, dtype=dt) for _ in range(ns)]
-        bw = [torch.empty(ws_bytes, device=dev, dtype=torch.uint8) for _ in range(ns)]
-        ready = torch.cuda.Event()
-        ready.record(main)  # state buffers / inputs on the main stream precede the copies
-        s_in.wait_event(ready)
-        in_done = [torch.cuda.Event() for _ in range(ngroups)]
-        comp_done = [torch.cuda.Event() for _ in range(ngroups)]
-        out_done = [torch.cuda.Event() for _ in range(ngroups)]
+        key = (mb, T, tuple(q.shape[2:]), H, Dv, dt, temp is not None, ws_bytes, ns)
+        pipe = _HOST_PIPES.get(dev)
+        if pipe is None or pipe.key != key:
+            _HOST_PIPES.pop(dev, None)
+            pipe = _HostPipeline(dev, key, mb, T, tuple(q.shape[1:]), H, Dv, dt, temp is not None, ws_bytes, ns)
+            _HOST_PIPES[dev] = pipe
+        s_in, s_out = pipe.s_in, pipe.s_out
+        if ordered:
+            ready = torch.cuda.Event()
+            ready.record(main)  # inputs and state on the caller's stream precede the copies
+            s_in.wait_event(ready)
+        last = None
         for j in range(ngroups):
             b0, b1 = j * mb, min(B, (j + 1) * mb)
             n = b1 - b0
             sl = j % ns
-            # host -> device (slot inputs free once the prefill that used them ended)
-            if j >= ns:
-                s_in.wait_event(comp_done[j - ns])
+            # host -> device, once the prefill that last read this slot is done
+            if pipe.in_free[sl] is not None:
+                s_in.wait_event(pipe.in_free[sl])
             with torch.cuda.stream(s_in):
-                bq[sl][:n].copy_(q[b0:b1], non_blocking=True)
-                bk[sl][:n].copy_(k[b0:b1], non_blocking=True)
-                bv[sl][:n].copy_(v[b0:b1], non_blocking=True)
+                pipe.bq[sl][:n].copy_(q[b0:b1], non_blocking=True)
+                pipe.bk[sl][:n].copy_(k[b0:b1], non_blocking=True)
+                pipe.bv[sl][:n].copy_(v[b0:b1], non_blocking=True)
                 if temp is not None:
-                    bt[sl][:n].copy_(temp[b0:b1], non_blocking=True)
-            in_done[j].record(s_in)
-            # fused prefill on the main stream (slot output free once copied out)
-            main.wait_event(in_done[j])
-            if j >= ns:
-                main.wait_event(out_done[j - ns])
+                    pipe.bt[sl][:n].copy_(temp[b0:b1], non_blocking=True)
+            in_done = torch.cuda.Event()
+            in_done.record(s_in)
+            # fused prefill on the caller's stream (slot output free once copied out)
+            main.wait_event(in_done)
+            if pipe.out_free[sl] is not None:
+                main.wait_event(pipe.out_free[sl])
             Sj = None if S is None else S[b0:b1]
             zj = None if z is None else z[b0:b1]
             _lib.check(L.fakla_prefill(
-                _ptr(bq[sl]), _ptr(bk[sl]), _ptr(bv[sl]), None if temp is None else _ptr(bt[sl]),
-                _ptr(weight), _ptr(bias), _ptr(bo[sl]), _ptr(Sj), _ptr(zj),
-                n, T, in_dim, H, M, Dv, code, flags, _ptr(bw[sl]), ws_bytes, main.cuda_stream))
-            comp_done[j].record(main)
+                _ptr(pipe.bq[sl]), _ptr(pipe.bk[sl]), _ptr(pipe.bv[sl]),
+                None if temp is None else _ptr(pipe.bt[sl]),
+                _ptr(weight), _ptr(bias), _ptr(pipe.bo[sl]), _ptr(Sj), _ptr(zj),
+                n, T, in_dim, H, M, Dv, code, flags, _ptr(pipe.bw[sl]), ws_bytes, main.cuda_stream))
+            comp = torch.cuda.Event()
+            comp.record(main)
+            pipe.in_free[sl] = comp
             # device -> host
-            s_out.wait_event(comp_done[j])
+            s_out.wait_event(comp)
             with torch.cuda.stream(s_out):
-                out[b0:b1].copy_(bo[sl][:n], non_blocking=True)
-            out_done[j].record(s_out)
-        # the caller's stream waits for the last copies; side-stream buffers stay
-        # reserved until then
-        main.wait_event(out_done[ngroups - 1])
-        for bufs in (bq, bk, bv, bo, bw) + ((bt,) if bt is not None else ()):
-            for t in bufs:
-                t.record_stream(s_in)
-                t.record_stream(s_out)
+                out[b0:b1].copy_(pipe.bo[sl][:n], non_blocking=True)
+            last = torch.cuda.Event()
+            last.record(s_out)
+            pipe.out_free[sl] = last
+        # the caller's stream waits for the last copies
+        main.wait_event(last)
     return out, ((S, z) if return_state else None)
 
 

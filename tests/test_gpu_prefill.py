@@ -193,6 +193,33 @@ def test_prefill_host_streaming_matches_device_and_oracle(cuda, micro_batch):
     assert rel_l2(to_np(S_h), eS) < BF16_REL_L2
 
 
+def test_prefill_host_back_to_back_unordered_calls(cuda):
+    """Consecutive fa_kla_host calls with ordered=False share the kept device
+    slots: each call's input copies wait only for the slot they refill. Four
+    calls on different inputs, queued without a synchronisation, each equal
+    the device call on their own inputs."""
+    from pulsartecture_b200.attention import fa_kla, fa_kla_host
+    from pulsartecture_b200.backend.interface import release_host_pipelines
+
+    B, T, H, D = 5, 260, 2, 128
+    W, b = lpm_params(H * D, H * D, seed=130, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    ins, outs = [], []
+    for c in range(4):
+        q = (gen((B, T, H, D), 131 + 3 * c) / np.sqrt(D)).bfloat16().pin_memory()
+        k = (gen((B, T, H, D), 132 + 3 * c) / np.sqrt(D)).bfloat16().pin_memory()
+        v = (gen((B, T, H, D), 133 + 3 * c) / np.sqrt(D)).bfloat16().pin_memory()
+        ins.append((q, k, v))
+    for q, k, v in ins:
+        o, _ = fa_kla_host(q, k, v, phi_weight=W, phi_bias=b, micro_batch=2, ordered=False)
+        outs.append(o)
+    torch.cuda.synchronize()
+    for (q, k, v), o in zip(ins, outs):
+        ref, _ = fa_kla(q.to(cuda), k.to(cuda), v.to(cuda), phi_weight=W, phi_bias=b)
+        assert rel_l2(to_np(o), to_np(ref)) < 2e-3
+    release_host_pipelines()
+
+
 def test_prefill_host_rejects_device_inputs(cuda):
     from pulsartecture_b200.attention import fa_kla_host
 
