@@ -249,13 +249,18 @@ class TMLinKernelAttn(nn.Module):
 
 def fa_kla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[State] = None, *,
            phi_weight: torch.Tensor, phi_bias: Optional[torch.Tensor] = None,
-           temp: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, State]:
+           temp: Optional[torch.Tensor] = None, chunk: int = 128) -> Tuple[torch.Tensor, State]:
     """Functional FA-KLA prefill with phi fused: ``forward(q, k, v, state) -> (out, state)``.
 
     q, k: (B, T, H_in, Dk) or (B, T, H_in*Dk) projected rows; v: (B, T, H, Dv);
     phi_weight: (H*M, H_in*Dk); phi_bias: (H*M,); temp: (B, T, H) or None.
-    The input state is not modified; a new (S, z) is returned.
+    The input state is not modified; a new (S, z) is returned. ``chunk`` is
+    accepted for chunked-scan call sites and must be positive; the kernels
+    tile by 128 tokens whatever it is (the result does not depend on the
+    chunk size beyond fp32 rounding).
     """
+    if chunk < 1:
+        raise RuntimeError(f"chunk must be positive, got {chunk}")
     out, st = fa_kla_prefill(q.contiguous(), k.contiguous(), v.contiguous(), phi_weight, phi_bias,
                              temp, state, True)
     return out, st
