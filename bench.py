@@ -428,12 +428,35 @@ def run_lm(args):
         h.remove()
     ms = e0.elapsed_time(e1) / args.steps
     attn_ms = sum(marks[i].elapsed_time(marks[i + 1]) for i in range(0, len(marks), 2)) / args.steps
+    # one training step: forward, next-token cross entropy, backward (FA-KLA
+    # through its tensor-core backward), no optimizer
+    targets = torch.randint(0, 32000, (B_, T_), generator=g, device=dev)
+
+    def train_step():
+        model.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.cross_entropy(model(ids).float().view(-1, 32000), targets.view(-1))
+        loss.backward()
+        return loss
+
+    for _ in range(2):
+        train_step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    n_train = max(2, min(args.steps, 5))
+    for _ in range(n_train):
+        loss = train_step()
+    t1.record()
+    t1.synchronize()
+    train_ms = t0.elapsed_time(t1) / n_train
     line = {"only": "lm", "model": "FA-KLA LM (this package's composition; no reference model exists)",
             "config": {"layers": 12, "d_model": 1024, "heads": 16, "head_dim": 64, "experts": "top-2 of 8",
                        "d_ff": 4096, "vocab": 32000, "batch": B_, "seq_len": T_, "dtype": "bf16"},
             "ms_per_forward": round(ms, 3), "tokens_per_s": round(B_ * T_ / ms * 1e3, 1),
             "fakla_ms_per_forward": round(attn_ms, 3), "fakla_share": round(attn_ms / ms, 4),
-            "logits_finite": bool(torch.isfinite(logits.float()).all().item())}
+            "logits_finite": bool(torch.isfinite(logits.float()).all().item()),
+            "train_step_ms": round(train_ms, 3), "train_tokens_per_s": round(B_ * T_ / train_ms * 1e3, 1),
+            "train_loss_finite": bool(torch.isfinite(loss).item())}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -355,7 +355,7 @@ extern "C" int fakla_attention_backward(const void* q, const void* k, const void
       workspace_bytes >= fakla::backward_sm100_workspace_bytes(B, T, H, d->sms)) {
     bool enc = false;
     cudaError_t e = fakla::launch_backward_sm100(q, k, v, temp, dout, S0, z0, dS_final, dz_final,
-                                                 dq, dk, dv, dtemp, dS0, dz0, B, T, H, workspace,
+                                                 dq, dk, dv, dtemp, dS0, dz0, B, T, H, Df, workspace,
                                                  d->sms, (cudaStream_t)stream, d->status, &enc);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "attention backward (sm100) launch");

@@ -71,14 +71,14 @@ cudaError_t launch_scan_sm100(const void* q, const void* k, const void* v, const
                               cudaStream_t stream, int* status, bool* encoded,
                               int64_t in_row_elems = 0, int64_t head_dim = 128);
 
-// Tensor-core backward (sm100_backward.cu): bf16, Df = Dv = 128.
+// Tensor-core backward (sm100_backward.cu): bf16, Df = Dv = 128 or 64.
 bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);
 size_t backward_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms);
 cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, const void* temp,
                                   const void* dout, const float* S0, const float* z0,
                                   const float* dS_final, const float* dz_final, void* dq, void* dk,
                                   void* dv, void* dtemp, float* dS0, float* dz0, int64_t B,
-                                  int64_t T, int64_t H, void* workspace, int sms,
+                                  int64_t T, int64_t H, int64_t hd, void* workspace, int sms,
                                   cudaStream_t stream, int* status, bool* encoded);
 // The backward scans (sm100_scan.cu, run by sm100_backward.cu). mode: 0 the
 // normalised forward (optionally writing den (B,T,H) and dden), 1 unnormalised causal with a per-row term `add` added to the kept q.k
@@ -108,7 +108,7 @@ cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, 
                                    void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                                    unsigned flags, const ScanBackwardArgs& m, void* workspace,
                                    size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
-                                   bool* encoded);
+                                   bool* encoded, int64_t head_dim = 128);
 // q/k/v GEMM: out (rows, 2*feat + vdim) = [phi(q) | phi(k) * temp | v] from
 // x (rows, K) and W (2*feat + vdim, K).
 bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads);

@@ -1,4 +1,4 @@
-// FA-KLA backward on tensor cores (bf16, Df = Dv = 128): the gradients of
+// FA-KLA backward on tensor cores (bf16, Df = Dv = 128 or 64): the gradients of
 // the recurrence of cpu_kernels.cpp:107-164 (simt_backward.cu states them)
 // as four chunked scans of sm100_scan.cu plus small fp32 passes.
 //
@@ -44,7 +44,7 @@
 namespace fakla {
 namespace {
 
-constexpr int D = 128;
+constexpr int D = 128;  // the widest head; heads of 64 use the same kernels
 constexpr int C = 128;  // scan chunk (tokens)
 
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
@@ -68,19 +68,20 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// One (b, t, h) row per 16 threads (8 values each): dnum = bf16(dout / den)
+// One (b, t, h) row per hd/8 threads (8 values each): dnum = bf16(dout / den)
 // (rounded as the forward scan's dden epilogue rounds it); with temp also
 // kc = k~ - m (k~ = k temp in fp32; m per sequence (b, h)).
 __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
                                 const float* __restrict__ den, const __nv_bfloat16* __restrict__ k,
                                 const __nv_bfloat16* __restrict__ temp, const float* __restrict__ m,
                                 __nv_bfloat16* __restrict__ dnum, __nv_bfloat16* __restrict__ kc,
-                                int64_t rows, int T, int H) {
+                                int64_t rows, int T, int H, int hd) {
+  const int parts = hd / 8;
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t row = gid >> 4;
-  const int part = (int)(gid & 15);
+  const int64_t row = gid / parts;
+  const int part = (int)(gid % parts);
   if (row >= rows) return;
-  const int64_t off = row * D + part * 8;
+  const int64_t off = row * hd + part * 8;
   float g[8];
   load8(dout + off, g);
   const float inv = 1.f / den[row];
@@ -93,72 +94,75 @@ __global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
     float kv[8];
     load8(k + off, kv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) kv[e] = kv[e] * tv - m[bh * D + part * 8 + e];
+    for (int e = 0; e < 8; ++e) kv[e] = kv[e] * tv - m[bh * hd + part * 8 + e];
     store8(kc + off, kv);
   }
 }
 
 // s[bh][c][f] = sum over the tokens t of chunk c of w_t x_t[f], w = wf (fp32),
 // else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t). Grid (nchunks,
-// B*H), 256 threads: 16 per token row (8 features each, 16-byte loads) over
-// 16 tokens at a time, then a shared memory reduction over the 16 token slots.
+// B*H), 256 threads: hd/8 per token row (8 features each, 16-byte loads) over
+// 256/(hd/8) tokens at a time, then a shared memory reduction over the token
+// slots.
 __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
                                       const float* __restrict__ wf,
                                       const __nv_bfloat16* __restrict__ wh, float* __restrict__ s,
-                                      __nv_bfloat16* __restrict__ wx, int T, int H) {
-  __shared__ float red[16][D + 4];
+                                      __nv_bfloat16* __restrict__ wx, int T, int H, int hd) {
+  __shared__ float red[32][D + 4];
+  const int parts = hd / 8;
+  const int nslots = 256 / parts;
   const int c = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
-  const int part = threadIdx.x & 15;  // features 8 part .. 8 part + 7
-  const int slot = threadIdx.x >> 4;  // token slot
+  const int part = threadIdx.x % parts;  // features 8 part .. 8 part + 7
+  const int slot = threadIdx.x / parts;  // token slot
   const int t1 = min(T, c * C + C);
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  for (int t = c * C + slot; t < t1; t += 16) {
+  for (int t = c * C + slot; t < t1; t += nslots) {
     const int64_t r = ((int64_t)b * T + t) * H + h;
     const float w = wf != nullptr ? wf[r] : (wh != nullptr ? __bfloat162float(wh[r]) : 1.f);
     float xv[8];
-    load8(x + r * D + part * 8, xv);
+    load8(x + r * hd + part * 8, xv);
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, xv[e], acc[e]);
     if (wx != nullptr) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) xv[e] *= w;
-      store8(wx + r * D + part * 8, xv);
+      store8(wx + r * hd + part * 8, xv);
     }
   }
 #pragma unroll
   for (int e = 0; e < 8; ++e) red[slot][part * 8 + e] = acc[e];
   __syncthreads();
-  if (threadIdx.x < D) {
+  if (threadIdx.x < hd) {
     float v = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v += red[i][threadIdx.x];
-    s[((int64_t)bh * gridDim.x + c) * D + threadIdx.x] = v;
+    for (int i = 0; i < nslots; ++i) v += red[i][threadIdx.x];
+    s[((int64_t)bh * gridDim.x + c) * hd + threadIdx.x] = v;
   }
 }
 
 // Exclusive prefix over the chunks (in place): s[c] <- init + sum_{c' < c} s[c'],
 // or with `reverse` the suffix init + sum_{c' > c} s[c']. total <- init + the
-// sum of all chunks, mean <- that sum / T (each if given). Grid B*H, 128 threads.
+// sum of all chunks, mean <- that sum / T (each if given). Grid B*H, hd threads.
 __global__ void bwd_scan_chunks_kernel(float* __restrict__ s, const float* __restrict__ init,
                                        float* __restrict__ total, float* __restrict__ mean,
                                        int nchunks, int T, int reverse) {
   const int64_t bh = blockIdx.x;
   const int f = threadIdx.x;
-  const float base_val = init != nullptr ? init[bh * D + f] : 0.f;
+  const int hd = blockDim.x;  // one thread per feature
+  const float base_val = init != nullptr ? init[bh * hd + f] : 0.f;
   float all = 0.f;
-  float* base = s + bh * nchunks * D + f;
+  float* base = s + bh * nchunks * hd + f;
   for (int i = 0; i < nchunks; ++i) {
     const int c = reverse ? nchunks - 1 - i : i;
-    const float v = base[(int64_t)c * D];
-    base[(int64_t)c * D] = base_val + all;
+    const float v = base[(int64_t)c * hd];
+    base[(int64_t)c * hd] = base_val + all;
     all += v;
   }
-  if (total != nullptr) total[bh * D + f] = base_val + all;
-  if (mean != nullptr) mean[bh * D + f] = all / (float)T;
+  if (total != nullptr) total[bh * hd + f] = base_val + all;
+  if (mean != nullptr) mean[bh * hd + f] = all / (float)T;
 }
 
 struct BwdLayout {
@@ -188,12 +192,13 @@ BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
 }  // namespace
 
 bool backward_sm100_supported(int dtype, int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv) {
-  return dtype == FAKLA_BF16 && Df == D && Dv == D && scan_sm100_supported(B, T, H, Df, Dv) &&
+  return dtype == FAKLA_BF16 && Df == Dv && (Df == D || Df == 64) && scan_sm100_supported(B, T, H, Df, Dv) &&
          B * T * H <= (int64_t)INT32_MAX;
 }
 
 size_t backward_sm100_workspace_bytes(int64_t B, int64_t T, int64_t H, int sms) {
-  // sized for the temp case (the k~ buffers); without temp they go unused
+  // sized for the temp case (the k~ buffers) and heads of 128; smaller heads
+  // and calls without temp use a part of it
   return bwd_layout(B, T, H, true, sms).total;
 }
 
@@ -201,7 +206,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                                   const void* dout, const float* S0, const float* z0,
                                   const float* dS_final, const float* dz_final, void* dq, void* dk,
                                   void* dv, void* dtemp, float* dS0, float* dz0, int64_t B,
-                                  int64_t T, int64_t H, void* workspace, int sms,
+                                  int64_t T, int64_t H, int64_t hd, void* workspace, int sms,
                                   cudaStream_t stream, int* status, bool* encoded) {
   const BwdLayout l = bwd_layout(B, T, H, temp != nullptr, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -224,9 +229,9 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   cudaError_t e;
 
   // 1. zb (z before each chunk, from z_0) and the mean of k~
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, (int)T, (int)H);
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, (int)T, (int)H, (int)hd);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(zb, z0, nullptr, mk, nch, (int)T, 0);
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(zb, z0, nullptr, mk, nch, (int)T, 0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   // 2. forward: den and dden (no output rows)
@@ -241,21 +246,22 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   const void* ktil = temp != nullptr ? (const void*)kt : k;
   e = launch_scan_sm100_mode(q, ktil, v, nullptr, nullptr, const_cast<float*>(S0),
                              const_cast<float*>(z0), B, T, H, in0, m, scan_ws, scan_bytes, sms,
-                             stream, status, encoded);
+                             stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
   // 3. W (suffix sums of dden q from dz_T) and dz_0
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, (int)T, (int)H);
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, (int)T, (int)H,
+                                                   (int)hd);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), D, 0, stream>>>(wq, dz_final, dz0, nullptr, nch,
-                                                              (int)T, 1);
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(wq, dz_final, dz0, nullptr,
+                                                                         nch, (int)T, 1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   // 4. dnum (and with temp k~ - m)
   {
-    const int64_t threads = rows * 16;
+    const int64_t threads = rows * (hd / 8);
     bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)dout, den, kh, th, mk, dnum, kc, rows, (int)T, (int)H);
+        (const __nv_bfloat16*)dout, den, kh, th, mk, dnum, kc, rows, (int)T, (int)H, (int)hd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
 
@@ -268,7 +274,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m.state_in_T = 1;
   e = launch_scan_sm100_mode(dnum, v, temp != nullptr ? (const void*)kc : k, nullptr, dq,
                              const_cast<float*>(S0), nullptr, B, T, H, in0, m, nullptr, 0, sms,
-                             stream, status, encoded);
+                             stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
   // 6. dk (and dtemp); before dv, whose final state may overwrite dS_T in place
@@ -284,7 +290,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   }
   const unsigned fk = dS_final != nullptr ? FAKLA_STATE_IN : 0u;
   e = launch_scan_sm100_mode(v, dnum, q, nullptr, dk, const_cast<float*>(dS_final), nullptr, B, T,
-                             H, fk, m, nullptr, 0, sms, stream, status, encoded);
+                             H, fk, m, nullptr, 0, sms, stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
   // 7. dv (and dS_0 as the reversed scan's final state)
@@ -295,7 +301,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
     fv |= FAKLA_STATE_OUT;
     if (dS_final != nullptr) {
       if (dS_final != dS0 &&
-          (e = cudaMemcpyAsync(dS0, dS_final, (size_t)(B * H) * D * D * sizeof(float),
+          (e = cudaMemcpyAsync(dS0, dS_final, (size_t)(B * H) * hd * hd * sizeof(float),
                                cudaMemcpyDeviceToDevice, stream)) != cudaSuccess)
         return e;
       fv |= FAKLA_STATE_IN;
@@ -307,7 +313,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m = ScanBackwardArgs{};
   m.mode = 2;
   return launch_scan_sm100_mode(ktil, q, dnum, nullptr, dv, Sv, nullptr, B, T, H, fv, m, nullptr, 0,
-                                sms, stream, status, encoded);
+                                sms, stream, status, encoded, hd);
 }
 
 }  // namespace fakla

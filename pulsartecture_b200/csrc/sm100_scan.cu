@@ -117,7 +117,7 @@ struct ScanArgs {
   unsigned flags;
   int* status;
   int hd;  // head size: 128, or 64 (features and values in the first 64 columns of
-           // each tile, whose second 64-column atom stays zero; kScanNormal only)
+           // each tile, whose second 64-column atom stays zero)
   // backward passes (modes below)
   const __nv_bfloat16* grad_rows;  // kScanNormalGrad: (B,T,H,D) output gradient -> dden_out (no output rows)
   float* dden_out;                 // (B,T,H): -(bf16(g/den) . out) (g = grad_rows)
@@ -500,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     constexpr int kPer = kAtom / 16;
     for (int o = threadIdx.x; o < 3 * kStages * kPer; o += kThreads) {
       const int t = o / kPer;  // Q0 Q1 K0 K1 V0 V1
+      // the unnormalised modes keep one K tile (the second K slot is Sb_lo)
+      if (kRaw && t == 3) continue;
       uint8_t* base = (t < 2 ? sQ : (t < 4 ? sK : sV)) + (t & 1) * kTile + kAtom;
       reinterpret_cast<uint4*>(base)[o % kPer] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -530,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         mbar_arrive_expect_tx(fb, 3 * na * kAtom);
         const int t0 = chunk_t0(i);
         if constexpr (kRaw) {
-          for (int a = 0; a < 2; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
+          for (int a = 0; a < na; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
           ++issued;
           // one K tile: MMA4 of the previous chunk must have read it
           if (i > 0 && !mbar_wait(&bars[kKFree], (uint32_t)(i - 1) & 1u, kWaitNs)) {
@@ -538,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
             *abort_flag = 1;
             break;
           }
-          for (int a = 0; a < 2; ++a) tma_load_4d(sK + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+          for (int a = 0; a < na; ++a) tma_load_4d(sK + a * kAtom, &tmK, fb, a * 64, h, t0, b);
         } else {
           for (int a = 0; a < na; ++a) {
             tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
@@ -725,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       } else if ((args.flags & FAKLA_STATE_IN) && args.S != nullptr && r < args.hd) {
         const int hd = args.hd;
         if (args.state_in_T)
-          scol = args.S + bh * D * D + r;
+          scol = args.S + bh * hd * hd + r;
         else
           srow = args.S + (bh * hd + r) * hd;
         srow_len = hd;
@@ -747,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           }
         } else if (scol != nullptr) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) f[e] = scol[(int64_t)(cc + e) * D];
+          for (int e = 0; e < 16; ++e) f[e] = cc + e < srow_len ? scol[(int64_t)(cc + e) * srow_len] : 0.f;
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) f[e] = 0.f;
@@ -837,7 +839,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     // barrier that ORs their wait results; every wait before it is bounded).
     const bool centre = MODE == kScanRowAdd && args.mvec != nullptr;
     if (kAffine) {
-      if (centre) (r < 64 ? mlo_sm[r] : mhi_sm[r - 64]) = args.mvec[(int64_t)bh_idx * D + r];
+      if (centre)
+        (r < 64 ? mlo_sm[r] : mhi_sm[r - 64]) = r < args.hd ? args.mvec[(int64_t)bh_idx * args.hd + r] : 0.f;
       named_barrier_sync(1, 128);
     }
     bool ok = true;
@@ -855,8 +858,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         wok = warp_wait(&bars[kBarS], par);
         if (wok && lane == 0) {
           uint64_t* rb = &bars[kRow0 + q4];
-          mbar_arrive_expect_tx(rb, 32 * 128 * 2);
-          for (int a = 0; a < 2; ++a)
+          mbar_arrive_expect_tx(rb, na * 32 * 64 * 2);
+          for (int a = 0; a < na; ++a)
             tma_load_4d(sQ + st * kTile + a * kAtom + q4 * (32 * 128), &tmR, rb, a * 64, h,
                         chunk_t0(i) + 32 * q4, b);
         }
@@ -865,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       // before the wait so that their latency overlaps MMA3
       float vval = 0.f, coef = 0.f, scale = 1.f;
       if (kAffine) {
-        vval = args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * D + r];
+        vval = r < args.hd ? args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * args.hd + r] : 0.f;
         coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
         if (args.row_scale != nullptr && live) scale = __bfloat162float(args.row_scale[row]);
       }
@@ -904,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         // no output rows
         float acc = 0.f;
 #pragma unroll 1
-        for (int cc = 0; cc < D; cc += 64) {
+        for (int cc = 0; cc < args.hd; cc += 64) {
           uint4 rh[8];
           load_row_smem(rtile, r, cc, rh);
           uint32_t va[32], vb[32];
@@ -940,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         constexpr bool kDot = MODE == kScanRevCol;
         float acc = 0.f;
 #pragma unroll 1
-        for (int cc = 0; cc < D; cc += 64) {
+        for (int cc = 0; cc < args.hd; cc += 64) {
           uint4 rh[8];
           if (kDot && row_tile) load_row_smem(rtile, r, cc, rh);
           uint32_t va[32], vb[32];
@@ -1294,7 +1297,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
                                     bool* encoded, int64_t in_row_elems, int64_t hd) {
   int mode = m != nullptr ? m->mode : kScanNormal;
   if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr) ||
-      (hd != D && (hd != 64 || m != nullptr)) ||
+      (hd != D && hd != 64) ||
       (mode == kScanNormal && m != nullptr && m->grad_rows != nullptr && m->dden_out == nullptr) ||
       ((mode == kScanRowAdd || mode == kScanRevCol) && (m->vec == nullptr || m->add == nullptr))) {
     *encoded = true;
@@ -1391,9 +1394,9 @@ cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, 
                                    void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,
                                    unsigned flags, const ScanBackwardArgs& m, void* workspace,
                                    size_t workspace_bytes, int sms, cudaStream_t stream, int* status,
-                                   bool* encoded) {
+                                   bool* encoded, int64_t head_dim) {
   return launch_scan_impl(q, k, v, temp, out, S, z, B, T, H, flags, &m, workspace, workspace_bytes,
-                          sms, stream, status, encoded, 0, D);
+                          sms, stream, status, encoded, 0, head_dim);
 }
 
 }  // namespace fakla

@@ -87,6 +87,7 @@ def test_attention_backward_bf16(cuda):
         assert rel_l2(to_np(t.grad), e) < BF16_REL_L2, name
 
 
+@pytest.mark.parametrize("D", [128, 64])
 @pytest.mark.parametrize("B,T,H,temp,state,final", [
     (1, 300, 3, True, True, True),     # ragged last chunk, every gradient
     (2, 129, 2, False, True, False),   # one token past a chunk, no temperature
@@ -94,13 +95,12 @@ def test_attention_backward_bf16(cuda):
     (1, 700, 2, True, False, True),    # six chunks, final-state gradients only
     (1, 128, 1, False, False, False),  # exactly one chunk
 ])
-def test_attention_backward_bf16_chunked(cuda, B, T, H, temp, state, final):
-    """bf16 128x128 heads take the tensor-core backward (chunked scans):
-    every gradient, including those of the initial state, against the
-    float64 oracle."""
+def test_attention_backward_bf16_chunked(cuda, B, T, H, temp, state, final, D):
+    """bf16 heads of 128 and 64 take the tensor-core backward (chunked
+    scans): every gradient, including those of the initial state, against
+    the float64 oracle."""
     from pulsartecture_b200.backend.interface import fa_kla_attention_with_state
 
-    D = 128
     args = _inputs(B, T, H, D, D, torch.bfloat16, cuda, 50 + T, temp, state)
     weights = _loss_weights(B, T, H, D, D, 60 + T)
     q, k, v, tp, S0, z0 = args
