@@ -236,8 +236,11 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         }
         const int c0 = col0 + j * 64;
         const bool ident = c0 >= args.ident_from;  // identity columns (the v block of a q/k/v GEMM)
+        // temperature on this chunk's columns (warp-uniform; rows past the end
+        // keep 1)
+        const bool scaled = temp != nullptr && c0 >= args.tcol0 && c0 < args.tcol1;
         float tscale = 1.f;
-        if (temp != nullptr && grow < args.rows && c0 >= args.tcol0 && c0 < args.tcol1)
+        if (scaled && grow < args.rows)
           tscale = __bfloat162float(temp[(int64_t)grow * args.heads + (c0 - args.tcol0) / m]);
         uint32_t bw[32];  // bias of the 64 columns as bf16 pairs (same for all lanes)
         if (args.bias != nullptr) {
@@ -272,8 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
               packed[i] = pack_bf16x2(fa * args.scale * tscale, fb * args.scale * tscale);
             } else if (ident) {
               packed[i] = pack_bf16x2(a, b);
-            } else {
+            } else if (scaled) {
               packed[i] = pack_bf16x2(activate<ACT, true>(a) * tscale, activate<ACT, true>(b) * tscale);
+            } else {
+              packed[i] = pack_bf16x2(activate<ACT, true>(a), activate<ACT, true>(b));
             }
           }
           // single staging buffer per warp: the previous store must have read it
