@@ -99,10 +99,12 @@ struct ScanBackwardArgs {
   const void* row_scale;
   const void* dot_rows;
   void* dot_out;  // bf16
-  // mode 0 with grad_rows: dden_out[t] = -(bf16(grad_rows[t] / den_t) . out_t),
-  // and no output rows are stored (out is not used)
+  // mode 0 with grad_rows: dden_out[t] = -(bf16(grad_rows[t] / den_t) . out_t);
+  // the output rows are not stored (out is not used), but dnum_out, if given,
+  // receives bf16(grad_rows[t] / den_t)
   const void* grad_rows;
   float* dden_out;
+  void* dnum_out;
 };
 cudaError_t launch_scan_sm100_mode(const void* q, const void* k, const void* v, const void* temp,
                                    void* out, float* S, float* z, int64_t B, int64_t T, int64_t H,

@@ -6,18 +6,19 @@
 // zb_c = z_0 + sum of k~ over the tokens before chunk c and
 // W_c = dz_T + sum of dden_t q_t over the tokens after chunk c:
 //
-//   1. sums of k~ per chunk  -> zb (prefix), m = mean of k~; k~ (bf16) with temp
-//   2. forward scan (mode 0) of (q, k~, v) -> den_t, and dden_t from its fp32 output
+//   1. m = mean of k~ over the first chunk; sums of k~ per chunk -> zb (prefix),
+//      and with temp k~ and k~ - m in bf16
+//   2. forward scan (mode 0) of (q, k~, v) -> den_t, dnum_t = bf16(dout_t / den_t),
+//      and dden_t from its fp32 output
 //   3. sums of dden q per chunk -> W (suffix), dz_0
-//   4. prep                  dnum, and with temp k~ - m (bf16)
-//   5. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m) with dden_t added
+//   4. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m) with dden_t added
 //            to row t of q'k'^T, initial state S_0^T; epilogue + dden_t zb_c
 //            + sigma_t m, sigma_t = the sum of row t of (q'k'^T + dden) over
 //            every key so far (the chunk's row sum + q'.z', z' = sum of v)
-//   6. dk~ = reversed scan of (q' = v, k' = dnum, v' = q) with dden_t added
+//   5. dk~ = reversed scan of (q' = v, k' = dnum, v' = q) with dden_t added
 //            to column t, initial state dS_T^T; epilogue + W_c, times temp_s
 //            -> dk; dtemp_s = dk~_s . k_s
-//   7. dv  = reversed scan of (q' = k~, k' = q, v' = dnum), initial state
+//   6. dv  = reversed scan of (q' = k~, k' = q, v' = dnum), initial state
 //            dS_T; its final state is dS_0
 //
 // Precision: for positive feature maps the products behind dq and dk~ cancel
@@ -68,46 +69,35 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// One (b, t, h) row per hd/8 threads (8 values each): dnum = bf16(dout / den)
-// (rounded as the forward scan's dden epilogue rounds it); with temp also
-// kc = k~ - m (k~ = k temp in fp32; m per sequence (b, h)).
-__global__ void bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
-                                const float* __restrict__ den, const __nv_bfloat16* __restrict__ k,
-                                const __nv_bfloat16* __restrict__ temp, const float* __restrict__ m,
-                                __nv_bfloat16* __restrict__ dnum, __nv_bfloat16* __restrict__ kc,
-                                int64_t rows, int T, int H, int hd) {
-  const int parts = hd / 8;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t row = gid / parts;
-  const int part = (int)(gid % parts);
-  if (row >= rows) return;
-  const int64_t off = row * hd + part * 8;
-  float g[8];
-  load8(dout + off, g);
-  const float inv = 1.f / den[row];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) g[e] *= inv;
-  store8(dnum + off, g);
-  if (temp != nullptr) {
-    const int64_t bh = (row / ((int64_t)T * H)) * H + row % H;
-    const float tv = __bfloat162float(temp[row]);
-    float kv[8];
-    load8(k + off, kv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) kv[e] = kv[e] * tv - m[bh * hd + part * 8 + e];
-    store8(kc + off, kv);
+// m[bh][f] = the mean of temp_t k_t[f] (fp32) over the first min(T, 128)
+// tokens of sequence bh: the centring vector of dq's v'. Grid B*H, hd threads.
+__global__ void bwd_first_chunk_mean_kernel(const __nv_bfloat16* __restrict__ k,
+                                            const __nv_bfloat16* __restrict__ temp,
+                                            float* __restrict__ m, int T, int H) {
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int hd = blockDim.x;
+  const int f = threadIdx.x;
+  const int n = min(T, C);
+  float acc = 0.f;
+  for (int t = 0; t < n; ++t) {
+    const int64_t r = ((int64_t)b * T + t) * H + h;
+    acc = fmaf(__bfloat162float(temp[r]), __bfloat162float(k[r * hd + f]), acc);
   }
+  m[(int64_t)bh * hd + f] = acc / (float)n;
 }
 
 // s[bh][c][f] = sum over the tokens t of chunk c of w_t x_t[f], w = wf (fp32),
-// else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t). Grid (nchunks,
+// else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t), and with wxc,
+// wxc_t = bf16(w_t x_t - mc[bh]) (w_t x_t in fp32). Grid (nchunks,
 // B*H), 256 threads: hd/8 per token row (8 features each, 16-byte loads) over
 // 256/(hd/8) tokens at a time, then a shared memory reduction over the token
 // slots.
 __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
                                       const float* __restrict__ wf,
                                       const __nv_bfloat16* __restrict__ wh, float* __restrict__ s,
-                                      __nv_bfloat16* __restrict__ wx, int T, int H, int hd) {
+                                      __nv_bfloat16* __restrict__ wx, const float* __restrict__ mc,
+                                      __nv_bfloat16* __restrict__ wxc, int T, int H, int hd) {
   __shared__ float red[32][D + 4];
   const int parts = hd / 8;
   const int nslots = 256 / parts;
@@ -131,6 +121,11 @@ __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
 #pragma unroll
       for (int e = 0; e < 8; ++e) xv[e] *= w;
       store8(wx + r * hd + part * 8, xv);
+      if (wxc != nullptr) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[e] -= mc[(int64_t)bh * hd + part * 8 + e];
+        store8(wxc + r * hd + part * 8, xv);
+      }
     }
   }
 #pragma unroll
@@ -166,7 +161,7 @@ __global__ void bwd_scan_chunks_kernel(float* __restrict__ s, const float* __res
 }
 
 struct BwdLayout {
-  size_t den, dden, dnum, kt, kc, zb, wq, mk, scan, total;
+  size_t dden, dnum, kt, kc, zb, wq, mk, scan, total;
 };
 
 BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
@@ -176,7 +171,6 @@ BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
   const size_t chunk_vecs = up((size_t)(B * H) * nch * D * 4);
   BwdLayout l;
   size_t o = 0;
-  l.den = o;  o += up(rows * 4);
   l.dden = o; o += up(rows * 4);
   l.dnum = o; o += up(rows * D * 2);
   l.kt = o;   o += temp ? up(rows * D * 2) : 0;
@@ -210,7 +204,6 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                                   cudaStream_t stream, int* status, bool* encoded) {
   const BwdLayout l = bwd_layout(B, T, H, temp != nullptr, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  auto* den = reinterpret_cast<float*>(ws + l.den);
   auto* dden = reinterpret_cast<float*>(ws + l.dden);
   auto* dnum = reinterpret_cast<__nv_bfloat16*>(ws + l.dnum);
   auto* kt = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kt) : nullptr;
@@ -220,7 +213,6 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   auto* mk = reinterpret_cast<float*>(ws + l.mk);
   void* scan_ws = ws + l.scan;
   const size_t scan_bytes = l.total - l.scan;
-  const int64_t rows = B * T * H;
   const int nch = (int)((T + C - 1) / C);
   const dim3 cgrid((unsigned)nch, (unsigned)(B * H));
   const auto* qh = static_cast<const __nv_bfloat16*>(q);
@@ -228,18 +220,24 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   const auto* th = static_cast<const __nv_bfloat16*>(temp);
   cudaError_t e;
 
-  // 1. zb (z before each chunk, from z_0) and the mean of k~
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, (int)T, (int)H, (int)hd);
+  // 1. the centring vector m (with temp), zb (z before each chunk, from z_0),
+  // and with temp k~ and k~ - m in bf16
+  if (temp != nullptr) {
+    bwd_first_chunk_mean_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(kh, th, mk, (int)T, (int)H);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, mk, kc, (int)T, (int)H, (int)hd);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(zb, z0, nullptr, mk, nch, (int)T, 0);
+  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(zb, z0, nullptr, nullptr, nch,
+                                                                         (int)T, 0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-  // 2. forward: den and dden (no output rows)
+  // 2. forward: dden and dnum (no output rows)
   ScanBackwardArgs m{};
   m.mode = 0;
-  m.den_out = den;
   m.grad_rows = dout;
   m.dden_out = dden;
+  m.dnum_out = dnum;
   const unsigned in0 = S0 != nullptr ? FAKLA_STATE_IN : 0u;
   // k~ is precomputed: the scan then skips its in-tile temp scaling, which
   // the P warps would otherwise do on the critical path of every chunk
@@ -250,22 +248,14 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   if (e != cudaSuccess) return e;
 
   // 3. W (suffix sums of dden q from dz_T) and dz_0
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, (int)T, (int)H,
-                                                   (int)hd);
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, nullptr, nullptr,
+                                                   (int)T, (int)H, (int)hd);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(wq, dz_final, dz0, nullptr,
                                                                          nch, (int)T, 1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
-  // 4. dnum (and with temp k~ - m)
-  {
-    const int64_t threads = rows * (hd / 8);
-    bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)dout, den, kh, th, mk, dnum, kc, rows, (int)T, (int)H, (int)hd);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-
-  // 5. dq
+  // 4. dq
   m = ScanBackwardArgs{};
   m.mode = 1;
   m.add = dden;
@@ -277,7 +267,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                              stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
-  // 6. dk (and dtemp); before dv, whose final state may overwrite dS_T in place
+  // 5. dk (and dtemp); before dv, whose final state may overwrite dS_T in place
   m = ScanBackwardArgs{};
   m.mode = 3;
   m.add = dden;
@@ -293,7 +283,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                              H, fk, m, nullptr, 0, sms, stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
-  // 7. dv (and dS_0 as the reversed scan's final state)
+  // 6. dv (and dS_0 as the reversed scan's final state)
   float* Sv = nullptr;
   unsigned fv = 0;
   if (dS0 != nullptr) {

@@ -119,8 +119,9 @@ struct ScanArgs {
   int hd;  // head size: 128, or 64 (features and values in the first 64 columns of
            // each tile, whose second 64-column atom stays zero)
   // backward passes (modes below)
-  const __nv_bfloat16* grad_rows;  // kScanNormalGrad: (B,T,H,D) output gradient -> dden_out (no output rows)
+  const __nv_bfloat16* grad_rows;  // kScanNormalGrad: (B,T,H,D) output gradient -> dden_out
   float* dden_out;                 // (B,T,H): -(bf16(g/den) . out) (g = grad_rows)
+  int dnum_store;                  // kScanNormalGrad: the output rows are bf16(g/den)
   const float* add;           // (B,T,H) per-token term added to the kept P entries, or null
   float* den_out;             // (B,T,H) denominators of the normalised mode, or null
   int state_in_T;             // the initial state is given transposed (S[dv][f])
@@ -321,18 +322,30 @@ __device__ __forceinline__ void load_row_smem(const uint8_t* tile, int r, int c0
     u[k] = *reinterpret_cast<const uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((c0 & 63) + 8 * k)));
 }
 
+// Half a row (64 bf16 from column c0) into a 128-row x 128-column
+// 128B-swizzled tile in shared memory (the layout load_row_smem reads).
+__device__ __forceinline__ void store_row_smem(uint8_t* tile, int r, int c0, const uint4 (&u)[8]) {
+  uint8_t* atom = tile + (c0 >= 64 ? kAtom : 0);
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((c0 & 63) + 8 * k))) = u[k];
+}
+
 // sum over 32 columns of bf16(g * inv) * (x * inv): x = out * den (fp32 bits
-// in v), g = 32 bf16 of the output gradient row (4 uint4). bf16(g * inv) is
-// rounded as bf16 pairs, exactly as the dnum tensor is stored.
-__device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, const uint4* g) {
+// in v), g = 32 bf16 of the output gradient row (4 uint4). g is replaced by
+// bf16(g * inv) (dnum, rounded as bf16 pairs), the value the sum uses.
+__device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, uint4* g) {
   float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float gf[8];
     bf16x8_to_f32(g[k], gf);
+    uint32_t* w = reinterpret_cast<uint32_t*>(&g[k]);
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
-      const float2 dn = __bfloat1622float2(__floats2bfloat162_rn(gf[e] * inv, gf[e + 1] * inv));
+      const __nv_bfloat162 d2 = __floats2bfloat162_rn(gf[e] * inv, gf[e + 1] * inv);
+      w[e / 2] = *reinterpret_cast<const uint32_t*>(&d2);
+      const float2 dn = __bfloat1622float2(d2);
       acc0 = fmaf(dn.x, __uint_as_float(v[8 * k + e]), acc0);
       acc1 = fmaf(dn.y, __uint_as_float(v[8 * k + e + 1]), acc1);
     }
@@ -904,7 +917,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       const uint8_t* rtile = sQ + st * kTile;
       if constexpr (kGrad) {
         // backward's forward pass: dden = -(bf16(g / den) . out), out in fp32;
-        // no output rows
+        // the output rows are dnum = bf16(g / den) (stored when asked for),
+        // written over g in the row tile that the store below reads
         float acc = 0.f;
 #pragma unroll 1
         for (int cc = 0; cc < args.hd; cc += 64) {
@@ -916,6 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           tmem_ld_wait();
           acc += dden_dot_32(va, inv, rh);
           acc += dden_dot_32(vb, inv, rh + 4);
+          if (args.dnum_store) store_row_smem(stg, r, cc, rh);
         }
         if (live) args.dden_out[row] = -acc;
       } else if (!kAffine) {
@@ -969,7 +984,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       __syncwarp();
       if (lane == 0) {
         const int t0 = chunk_t0(i) + 32 * q4;
-        if (t0 < args.T && !kGrad) {
+        if (t0 < args.T && (!kGrad || args.dnum_store)) {
           for (int a = 0; a < na; ++a)
             tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
           bulk_commit_group();
@@ -1308,7 +1323,8 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   // stored then) or the dot rows of mode 3.
   const void* rows = mode == kScanNormalGrad ? m->grad_rows
                      : (mode == kScanRevCol && m->dot_out != nullptr ? m->dot_rows : nullptr);
-  if (mode == kScanNormalGrad) out = const_cast<void*>(rows);
+  if (mode == kScanNormalGrad && m->dnum_out == nullptr) out = const_cast<void*>(rows);
+  if (mode == kScanNormalGrad && m->dnum_out != nullptr) out = m->dnum_out;
   CUtensorMap mQ, mK, mV, mO, mR;
   const bool ok = make_map_bthd(&mQ, q, B, T, H, C, in_row_elems, hd) &&
                   make_map_bthd(&mK, k, B, T, H, C, in_row_elems, hd) &&
@@ -1369,6 +1385,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   a.dot_rows = m ? static_cast<const __nv_bfloat16*>(m->dot_rows) : nullptr;
   a.dot_out = m ? static_cast<__nv_bfloat16*>(m->dot_out) : nullptr;
   a.grad_rows = m ? static_cast<const __nv_bfloat16*>(m->grad_rows) : nullptr;
+  a.dnum_store = (m != nullptr && m->dnum_out != nullptr) ? 1 : 0;
   a.mvec = m ? m->mvec : nullptr;
   a.dden_out = m ? m->dden_out : nullptr;
   const int64_t ctas = B * H * G;
