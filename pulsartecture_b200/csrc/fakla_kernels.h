@@ -94,7 +94,10 @@ struct ScanBackwardArgs {
   const float* add;
   float* den_out;
   int state_in_T;
-  const float* vec;   // modes 1, 3: required
+  const float* vec;   // modes 1, 3: required; per-chunk sums, accumulated by the scan in
+                      // its walking order from vec_init (or 0) before each chunk
+  const float* vec_init;  // (B*H, D) or null
+  float* vec_total;       // (B*H, D): vec_init + all chunk sums, or null
   const float* mvec;  // mode 1: v' was centred by this (B*H, D) vector, or null
   const void* row_scale;
   const void* dot_rows;

@@ -6,11 +6,12 @@
 // zb_c = z_0 + sum of k~ over the tokens before chunk c and
 // W_c = dz_T + sum of dden_t q_t over the tokens after chunk c:
 //
-//   1. m = mean of k~ over the first chunk; sums of k~ per chunk -> zb (prefix),
-//      and with temp k~ and k~ - m in bf16
+//   1. m = mean of k~ over the first chunk; sums of k~ per chunk (zb is their
+//      prefix from z_0, formed by dq's scan), and with temp k~ and k~ - m in bf16
 //   2. forward scan (mode 0) of (q, k~, v) -> den_t, dnum_t = bf16(dout_t / den_t),
 //      and dden_t from its fp32 output
-//   3. sums of dden q per chunk -> W (suffix), dz_0
+//   3. sums of dden q per chunk (W is their suffix from dz_T, formed by dk~'s
+//      scan, which also writes dz_0)
 //   4. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m) with dden_t added
 //            to row t of q'k'^T, initial state S_0^T; epilogue + dden_t zb_c
 //            + sigma_t m, sigma_t = the sum of row t of (q'k'^T + dden) over
@@ -69,27 +70,9 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// m[bh][f] = the mean of temp_t k_t[f] (fp32) over the first min(T, 128)
-// tokens of sequence bh: the centring vector of dq's v'. Grid B*H, hd threads.
-__global__ void bwd_first_chunk_mean_kernel(const __nv_bfloat16* __restrict__ k,
-                                            const __nv_bfloat16* __restrict__ temp,
-                                            float* __restrict__ m, int T, int H) {
-  const int bh = blockIdx.x;
-  const int b = bh / H, h = bh % H;
-  const int hd = blockDim.x;
-  const int f = threadIdx.x;
-  const int n = min(T, C);
-  float acc = 0.f;
-  for (int t = 0; t < n; ++t) {
-    const int64_t r = ((int64_t)b * T + t) * H + h;
-    acc = fmaf(__bfloat162float(temp[r]), __bfloat162float(k[r * hd + f]), acc);
-  }
-  m[(int64_t)bh * hd + f] = acc / (float)n;
-}
-
-// s[bh][c][f] = sum over the tokens t of chunk c of w_t x_t[f], w = wf (fp32),
-// else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t), and with wxc,
-// wxc_t = bf16(w_t x_t - mc[bh]) (w_t x_t in fp32). Grid (nchunks,
+// s[bh][c][f] = scale * the sum over the tokens t of chunk c of w_t x_t[f],
+// w = wf (fp32), else wh (bf16), else 1; with wx, also wx_t = bf16(w_t x_t),
+// and with wxc, wxc_t = bf16(w_t x_t - mc[bh]) (w_t x_t in fp32). Grid (nchunks,
 // B*H), 256 threads: hd/8 per token row (8 features each, 16-byte loads) over
 // 256/(hd/8) tokens at a time, then a shared memory reduction over the token
 // slots.
@@ -97,7 +80,8 @@ __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
                                       const float* __restrict__ wf,
                                       const __nv_bfloat16* __restrict__ wh, float* __restrict__ s,
                                       __nv_bfloat16* __restrict__ wx, const float* __restrict__ mc,
-                                      __nv_bfloat16* __restrict__ wxc, int T, int H, int hd) {
+                                      __nv_bfloat16* __restrict__ wxc, int T, int H, int hd,
+                                      float scale) {
   __shared__ float red[32][D + 4];
   const int parts = hd / 8;
   const int nslots = 256 / parts;
@@ -134,30 +118,8 @@ __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
   if (threadIdx.x < hd) {
     float v = 0.f;
     for (int i = 0; i < nslots; ++i) v += red[i][threadIdx.x];
-    s[((int64_t)bh * gridDim.x + c) * hd + threadIdx.x] = v;
+    s[((int64_t)bh * gridDim.x + c) * hd + threadIdx.x] = v * scale;
   }
-}
-
-// Exclusive prefix over the chunks (in place): s[c] <- init + sum_{c' < c} s[c'],
-// or with `reverse` the suffix init + sum_{c' > c} s[c']. total <- init + the
-// sum of all chunks, mean <- that sum / T (each if given). Grid B*H, hd threads.
-__global__ void bwd_scan_chunks_kernel(float* __restrict__ s, const float* __restrict__ init,
-                                       float* __restrict__ total, float* __restrict__ mean,
-                                       int nchunks, int T, int reverse) {
-  const int64_t bh = blockIdx.x;
-  const int f = threadIdx.x;
-  const int hd = blockDim.x;  // one thread per feature
-  const float base_val = init != nullptr ? init[bh * hd + f] : 0.f;
-  float all = 0.f;
-  float* base = s + bh * nchunks * hd + f;
-  for (int i = 0; i < nchunks; ++i) {
-    const int c = reverse ? nchunks - 1 - i : i;
-    const float v = base[(int64_t)c * hd];
-    base[(int64_t)c * hd] = base_val + all;
-    all += v;
-  }
-  if (total != nullptr) total[bh * hd + f] = base_val + all;
-  if (mean != nullptr) mean[bh * hd + f] = all / (float)T;
 }
 
 struct BwdLayout {
@@ -220,16 +182,17 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   const auto* th = static_cast<const __nv_bfloat16*>(temp);
   cudaError_t e;
 
-  // 1. the centring vector m (with temp), zb (z before each chunk, from z_0),
-  // and with temp k~ and k~ - m in bf16
+  // 1. with temp the centring vector m (the first chunk's mean of k~), then
+  // the sums of k~ per chunk (dq's scan turns them into zb as it walks the
+  // chunks), and with temp k~ and k~ - m in bf16
   if (temp != nullptr) {
-    bwd_first_chunk_mean_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(kh, th, mk, (int)T, (int)H);
+    bwd_chunk_sums_kernel<<<dim3(1u, (unsigned)(B * H)), 256, 0, stream>>>(
+        kh, nullptr, th, mk, nullptr, nullptr, nullptr, (int)T, (int)H, (int)hd,
+        1.f / (float)(T < C ? T : C));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, mk, kc, (int)T, (int)H, (int)hd);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(zb, z0, nullptr, nullptr, nch,
-                                                                         (int)T, 0);
+  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(kh, nullptr, th, zb, kt, mk, kc, (int)T, (int)H,
+                                                   (int)hd, 1.f);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   // 2. forward: dden and dnum (no output rows)
@@ -247,12 +210,10 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                              stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
-  // 3. W (suffix sums of dden q from dz_T) and dz_0
+  // 3. the sums of dden q per chunk (dk~'s scan turns them into W walking
+  // from the end, and writes dz_0)
   bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, nullptr, nullptr,
-                                                   (int)T, (int)H, (int)hd);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  bwd_scan_chunks_kernel<<<(unsigned)(B * H), (unsigned)hd, 0, stream>>>(wq, dz_final, dz0, nullptr,
-                                                                         nch, (int)T, 1);
+                                                   (int)T, (int)H, (int)hd, 1.f);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   // 4. dq
@@ -260,6 +221,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m.mode = 1;
   m.add = dden;
   m.vec = zb;
+  m.vec_init = z0;
   m.mvec = temp != nullptr ? mk : nullptr;
   m.state_in_T = 1;
   e = launch_scan_sm100_mode(dnum, v, temp != nullptr ? (const void*)kc : k, nullptr, dq,
@@ -272,6 +234,8 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m.mode = 3;
   m.add = dden;
   m.vec = wq;
+  m.vec_init = dz_final;
+  m.vec_total = dz0;
   m.state_in_T = 1;
   m.row_scale = temp;
   if (temp != nullptr && dtemp != nullptr) {

@@ -125,11 +125,14 @@ struct ScanArgs {
   const float* add;           // (B,T,H) per-token term added to the kept P entries, or null
   float* den_out;             // (B,T,H) denominators of the normalised mode, or null
   int state_in_T;             // the initial state is given transposed (S[dv][f])
-  // backward epilogues: out = (o + coef * vec[chunk] + sigma_t mvec) * row_scale,
+  // backward epilogues: out = (o + coef * vec_c + sigma_t mvec) * row_scale, vec_c =
+  // vec_init + the sums of the chunks walked before chunk c,
   // coef = add[t] in kScanRowAdd and 1 in kScanRevCol, sigma_t = the row's
   // kept q'.k' + term summed over all chunks so far (the centring term of
   // v' = v - mvec); dot_out[t] = sum(that unscaled row * dot_rows[t])
-  const float* vec;           // (B*H, nchunks, D), or null
+  const float* vec;           // (B*H, nchunks, hd) per-chunk sums, or null
+  const float* vec_init;      // (B*H, hd): the vector before the first chunk walked, or null (0)
+  float* vec_total;           // (B*H, hd): vec_init + every chunk's sum, or null
   const float* mvec;          // (B*H, D), or null
   const __nv_bfloat16* row_scale;  // (B,T,H), or null
   const __nv_bfloat16* dot_rows;   // (B,T,H,D) with dot_out, or null
@@ -856,7 +859,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         (r < 64 ? mlo_sm[r] : mhi_sm[r - 64]) = r < args.hd ? args.mvec[(int64_t)bh_idx * args.hd + r] : 0.f;
       named_barrier_sync(1, 128);
     }
+    // running chunk vector of the affine modes (feature r)
+    float run = (kAffine && r < args.hd && args.vec_init != nullptr)
+                    ? args.vec_init[(int64_t)bh_idx * args.hd + r] : 0.f;
     bool ok = true;
+    int done = 0;
     for (int i = 0; i < nch && (kAffine || !warp_aborted(abort_flag)); ++i) {
       const uint32_t par = (uint32_t)i & 1u;
       const int t_tok = chunk_t0(i) + r;
@@ -881,7 +888,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       // before the wait so that their latency overlaps MMA3
       float vval = 0.f, coef = 0.f, scale = 1.f;
       if (kAffine) {
-        vval = r < args.hd ? args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * args.hd + r] : 0.f;
+        vval = run;
+        if (r < args.hd) run += args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * args.hd + r];
         coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
         if (args.row_scale != nullptr && live) scale = __bfloat162float(args.row_scale[row]);
       }
@@ -994,7 +1002,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (kStageInV) mbar_arrive(&bars[kEmpty0 + st]);  // ... and the V tile
       }
       __syncwarp();
+      ++done;
     }
+    // every chunk walked: the vector's total
+    if (kAffine && done == nch && args.vec_total != nullptr && r < args.hd)
+      args.vec_total[(int64_t)bh_idx * args.hd + r] = run;
     if (lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
     if (!ok) {
       report_status(args.status, FAKLA_ERR_TIMEOUT);
@@ -1387,6 +1399,8 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   a.grad_rows = m ? static_cast<const __nv_bfloat16*>(m->grad_rows) : nullptr;
   a.dnum_store = (m != nullptr && m->dnum_out != nullptr) ? 1 : 0;
   a.mvec = m ? m->mvec : nullptr;
+  a.vec_init = m ? m->vec_init : nullptr;
+  a.vec_total = m ? m->vec_total : nullptr;
   a.dden_out = m ? m->dden_out : nullptr;
   const int64_t ctas = B * H * G;
   switch (mode) {
