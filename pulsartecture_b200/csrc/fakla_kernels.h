@@ -98,6 +98,8 @@ struct ScanBackwardArgs {
                       // its walking order from vec_init (or 0) before each chunk
   const float* vec_init;  // (B*H, D) or null
   float* vec_total;       // (B*H, D): vec_init + all chunk sums, or null
+  int vec_mma;            // mode 3: the chunk sums are v'^T add, formed on the tensor cores
+                          // (vec is then not read)
   const float* mvec;  // mode 1: v' was centred by this (B*H, D) vector, or null
   const void* row_scale;
   const void* dot_rows;

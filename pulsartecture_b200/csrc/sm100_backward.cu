@@ -10,8 +10,8 @@
 //      prefix from z_0, formed by dq's scan), and with temp k~ and k~ - m in bf16
 //   2. forward scan (mode 0) of (q, k~, v) -> den_t, dnum_t = bf16(dout_t / den_t),
 //      and dden_t from its fp32 output
-//   3. sums of dden q per chunk (W is their suffix from dz_T, formed by dk~'s
-//      scan, which also writes dz_0)
+//   3. (none: dk~'s scan forms W, the suffix of the per-chunk sums of dden q
+//      from dz_T, with one extra MMA per chunk, and writes dz_0)
 //   4. dq  = causal scan of (q' = dnum, k' = v, v' = k~ - m) with dden_t added
 //            to row t of q'k'^T, initial state S_0^T; epilogue + dden_t zb_c
 //            + sigma_t m, sigma_t = the sum of row t of (q'k'^T + dden) over
@@ -123,7 +123,7 @@ __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
 }
 
 struct BwdLayout {
-  size_t dden, dnum, kt, kc, zb, wq, mk, scan, total;
+  size_t dden, dnum, kt, kc, zb, mk, scan, total;
 };
 
 BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
@@ -138,7 +138,6 @@ BwdLayout bwd_layout(int64_t B, int64_t T, int64_t H, bool temp, int sms) {
   l.kt = o;   o += temp ? up(rows * D * 2) : 0;
   l.kc = o;   o += temp ? up(rows * D * 2) : 0;
   l.zb = o;   o += chunk_vecs;
-  l.wq = o;   o += chunk_vecs;
   l.mk = o;   o += up((size_t)(B * H) * D * 4);
   l.scan = o; o += up(scan_sm100_workspace_bytes(B, T, H, sms));
   l.total = o;
@@ -171,13 +170,11 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   auto* kt = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kt) : nullptr;
   auto* kc = temp != nullptr ? reinterpret_cast<__nv_bfloat16*>(ws + l.kc) : nullptr;
   auto* zb = reinterpret_cast<float*>(ws + l.zb);
-  auto* wq = reinterpret_cast<float*>(ws + l.wq);
   auto* mk = reinterpret_cast<float*>(ws + l.mk);
   void* scan_ws = ws + l.scan;
   const size_t scan_bytes = l.total - l.scan;
   const int nch = (int)((T + C - 1) / C);
   const dim3 cgrid((unsigned)nch, (unsigned)(B * H));
-  const auto* qh = static_cast<const __nv_bfloat16*>(q);
   const auto* kh = static_cast<const __nv_bfloat16*>(k);
   const auto* th = static_cast<const __nv_bfloat16*>(temp);
   cudaError_t e;
@@ -210,11 +207,6 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
                              stream, status, encoded, hd);
   if (e != cudaSuccess) return e;
 
-  // 3. the sums of dden q per chunk (dk~'s scan turns them into W walking
-  // from the end, and writes dz_0)
-  bwd_chunk_sums_kernel<<<cgrid, 256, 0, stream>>>(qh, dden, nullptr, wq, nullptr, nullptr, nullptr,
-                                                   (int)T, (int)H, (int)hd, 1.f);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
 
   // 4. dq
   m = ScanBackwardArgs{};
@@ -233,7 +225,7 @@ cudaError_t launch_backward_sm100(const void* q, const void* k, const void* v, c
   m = ScanBackwardArgs{};
   m.mode = 3;
   m.add = dden;
-  m.vec = wq;
+  m.vec_mma = 1;  // W: the chunk sums of dden q come from the scan's own MMAs
   m.vec_init = dz_final;
   m.vec_total = dz0;
   m.state_in_T = 1;

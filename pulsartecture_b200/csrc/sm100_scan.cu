@@ -133,6 +133,7 @@ struct ScanArgs {
   const float* vec;           // (B*H, nchunks, hd) per-chunk sums, or null
   const float* vec_init;      // (B*H, hd): the vector before the first chunk walked, or null (0)
   float* vec_total;           // (B*H, hd): vec_init + every chunk's sum, or null
+  int vec_mma;                // kScanRevCol: the chunk sums are v'^T add, on the tensor cores
   const float* mvec;          // (B*H, D), or null
   const __nv_bfloat16* row_scale;  // (B,T,H), or null
   const __nv_bfloat16* dot_rows;   // (B,T,H,D) with dot_out, or null
@@ -647,6 +648,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           mma_ts(tmem + kColO, tmem + col, mndesc(aV, j), idPV, 1u);
           mma_ts(tmem + kColO, tmem + col + 16u, mndesc(aV, j), idPV, 1u);
         }
+        if constexpr (MODE == kScanRevCol) {
+          if (args.vec_mma) {
+            // MMA-W: sum over the chunk's tokens of v'_t add_t, one N=16 slot per
+            // chunk parity (columns 0 and 1: the hi and lo parts of add)
+            const uint32_t slot = tmem + kColZ + 16u * ((uint32_t)i & 1u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              mma_ss(slot, mndesc(aV, j),
+                     smem_desc_sw128(aM0 + 768u + (uint32_t)((j >> 2) * 1024 + (j & 3) * 32), 16, kSmallSbo),
+                     idK1, j > 0 ? 1u : 0u);
+          }
+        }
         mma_commit(&bars[kBarO]);
         if constexpr (!kStageInV) mma_commit(&bars[kEmpty0 + st]);
       }
@@ -681,6 +694,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       if constexpr (kCol) {
         if (named_barrier_or(2, 128, !ok || *abort_flag != 0)) break;
         bcol_sm[r] = bval;  // the previous chunk's readers passed the barrier above
+        if (args.vec_mma) {
+          // the column terms as the B operand of MMA-W: bf16 hi in row 6, lo in
+          // row 7 of M0 (tokens 0-63) and M1 (tokens 64-127); MMA-W of the
+          // previous chunk completed before barP
+          const __nv_bfloat16 bh16 = __float2bfloat16_rn(bval);
+          const __nv_bfloat16 bl16 = __float2bfloat16_rn(bval - __bfloat162float(bh16));
+          uint8_t* blk = sM0 + (r >= 64 ? 1024 : 0);
+          *reinterpret_cast<__nv_bfloat16*>(blk + sw128_offset(6, (uint32_t)(r & 63))) = bh16;
+          *reinterpret_cast<__nv_bfloat16*>(blk + sw128_offset(7, (uint32_t)(r & 63))) = bl16;
+          fence_proxy_async_smem();
+        }
         named_barrier_sync(2, 128);
       } else if (!ok) {
         break;
@@ -889,7 +913,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       float vval = 0.f, coef = 0.f, scale = 1.f;
       if (kAffine) {
         vval = run;
-        if (r < args.hd) run += args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * args.hd + r];
+        if (!args.vec_mma && r < args.hd)
+          run += args.vec[((int64_t)bh_idx * nchunks_total + chunk_t0(i) / C) * args.hd + r];
         coef = MODE == kScanRowAdd ? (live ? args.add[row] : 0.f) : 1.f;
         if (args.row_scale != nullptr && live) scale = __bfloat162float(args.row_scale[row]);
       }
@@ -899,6 +924,15 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (named_barrier_or(1, 128, !wok || *abort_flag != 0)) {
           ok = wok;
           break;
+        }
+        if (MODE == kScanRevCol && args.vec_mma) {
+          // this chunk's sum (MMA-W, complete with barO) joins the running
+          // vector after this chunk's own value was taken
+          tc_fence_after();
+          uint32_t w0, w1;
+          tmem_ld2(lane_addr + kColZ + 16u * ((uint32_t)i & 1u), w0, w1);
+          tmem_ld_wait();
+          run += __uint_as_float(w0) + __uint_as_float(w1);
         }
         vec_sm[r] = vval;  // the previous chunk's readers passed the barrier above
         named_barrier_sync(1, 128);
@@ -1326,7 +1360,8 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   if (mode < kScanNormal || mode > kScanRevCol || (mode != kScanNormal && temp != nullptr) ||
       (hd != D && hd != 64) ||
       (mode == kScanNormal && m != nullptr && m->grad_rows != nullptr && m->dden_out == nullptr) ||
-      ((mode == kScanRowAdd || mode == kScanRevCol) && (m->vec == nullptr || m->add == nullptr))) {
+      ((mode == kScanRowAdd || mode == kScanRevCol) && m->add == nullptr) ||
+      ((mode == kScanRowAdd || mode == kScanRevCol) && m->vec == nullptr && !(mode == kScanRevCol && m->vec_mma))) {
     *encoded = true;
     return cudaErrorInvalidValue;
   }
@@ -1401,6 +1436,7 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
   a.mvec = m ? m->mvec : nullptr;
   a.vec_init = m ? m->vec_init : nullptr;
   a.vec_total = m ? m->vec_total : nullptr;
+  a.vec_mma = (m != nullptr && m->vec_mma) ? 1 : 0;
   a.dden_out = m ? m->dden_out : nullptr;
   const int64_t ctas = B * H * G;
   switch (mode) {
