@@ -98,6 +98,15 @@ def _state_buffers(state: Optional[State], return_state: bool, B, H, Df, Dv, dev
     return S, z, flags
 
 
+def _no_tokens(out, state: Optional[State], S, z, return_state: bool):
+    """The result of a call over zero tokens: the output as allocated (empty)
+    and the input state unchanged, or the zero state."""
+    if return_state and state is None:
+        S.zero_()
+        z.zero_()
+    return out, ((S, z) if return_state else None)
+
+
 def fa_kla_attention_with_state(q_mapped: torch.Tensor, k_mapped: torch.Tensor, v_reshaped: torch.Tensor,
                                 temp: Optional[torch.Tensor] = None, state: Optional[State] = None,
                                 return_state: bool = True):
@@ -131,7 +140,7 @@ def fa_kla_attention_with_state(q_mapped: torch.Tensor, k_mapped: torch.Tensor, 
     out = torch.empty_like(v_reshaped)
     S, z, flags = _state_buffers(state, return_state, B, H, Df, Dv, dev)
     if B * T * H == 0:
-        return out, ((S, z) if return_state else None)
+        return _no_tokens(out, state, S, z, return_state)
     L = _lib.lib()
     with torch.cuda.device(dev):
         # segment records of the tensor-core scan (0 bytes unless few (b, h)
@@ -227,7 +236,7 @@ def fa_kla_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: to
     out = torch.empty(B, T, H, Dv, device=dev, dtype=dt)
     S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
     if B * T == 0:
-        return out, ((S, z) if return_state else None)
+        return _no_tokens(out, state, S, z, return_state)
     L = _lib.lib()
     ws_bytes = L.fakla_prefill_workspace_bytes(B, T, in_dim, H, M, Dv, code)
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
@@ -385,7 +394,7 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
              "out must be a contiguous (B, T, H, Dv) host tensor of the input dtype")
     S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
     if B * T == 0:
-        return out, ((S, z) if return_state else None)
+        return _no_tokens(out, state, S, z, return_state)
     L = _lib.lib()
     mb = min(micro_batch, B)
     ngroups = (B + mb - 1) // mb
@@ -714,7 +723,7 @@ def fa_kla_qkv_prefill(x: torch.Tensor, weight: torch.Tensor, bias: Optional[tor
     out = torch.empty(B, T, H, Dv, device=dev, dtype=dt)
     S, z, flags = _state_buffers(state, return_state, B, H, M, Dv, dev)
     if B * T == 0:
-        return out, ((S, z) if return_state else None)
+        return _no_tokens(out, state, S, z, return_state)
     L = _lib.lib()
     with torch.cuda.device(dev):
         ws_bytes = L.fakla_qkv_prefill_workspace_bytes(B, T, E, H, M, Dv, code)

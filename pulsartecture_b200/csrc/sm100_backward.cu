@@ -94,21 +94,37 @@ __global__ void bwd_chunk_sums_kernel(const __nv_bfloat16* __restrict__ x,
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  for (int t = c * C + slot; t < t1; t += nslots) {
-    const int64_t r = ((int64_t)b * T + t) * H + h;
-    const float w = wf != nullptr ? wf[r] : (wh != nullptr ? __bfloat162float(wh[r]) : 1.f);
-    float xv[8];
-    load8(x + r * hd + part * 8, xv);
+  float mv[8];  // the centring vector's 8 features (with wxc)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, xv[e], acc[e]);
+  for (int e = 0; e < 8; ++e) mv[e] = wxc != nullptr ? mc[(int64_t)bh * hd + part * 8 + e] : 0.f;
+  // two tokens per step, both loads issued before either is used
+  for (int t = c * C + slot; t < t1; t += 2 * nslots) {
+    const bool two = t + nslots < t1;
+    const int64_t r0 = ((int64_t)b * T + t) * H + h;
+    const int64_t r1 = two ? r0 + (int64_t)nslots * H : r0;
+    const float w0 = wf != nullptr ? wf[r0] : (wh != nullptr ? __bfloat162float(wh[r0]) : 1.f);
+    const float w1 = !two ? 0.f : (wf != nullptr ? wf[r1] : (wh != nullptr ? __bfloat162float(wh[r1]) : 1.f));
+    float x0[8], x1[8];
+    load8(x + r0 * hd + part * 8, x0);
+    load8(x + r1 * hd + part * 8, x1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = fmaf(w1, x1[e], fmaf(w0, x0[e], acc[e]));
     if (wx != nullptr) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xv[e] *= w;
-      store8(wx + r * hd + part * 8, xv);
+      for (int e = 0; e < 8; ++e) {
+        x0[e] *= w0;
+        x1[e] *= w1;
+      }
+      store8(wx + r0 * hd + part * 8, x0);
+      if (two) store8(wx + r1 * hd + part * 8, x1);
       if (wxc != nullptr) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xv[e] -= mc[(int64_t)bh * hd + part * 8 + e];
-        store8(wxc + r * hd + part * 8, xv);
+        for (int e = 0; e < 8; ++e) {
+          x0[e] -= mv[e];
+          x1[e] -= mv[e];
+        }
+        store8(wxc + r0 * hd + part * 8, x0);
+        if (two) store8(wxc + r1 * hd + part * 8, x1);
       }
     }
   }

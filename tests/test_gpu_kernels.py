@@ -250,3 +250,32 @@ def test_decode_fused_phi_bf16(cuda):
     assert rel_l2(to_np(out), eo) < BF16_REL_L2
     assert np.abs(to_np(out) - eo).max() < BF16_MAX_ABS
     assert rel_l2(to_np(S), eS) < BF16_REL_L2 and rel_l2(to_np(z), ez) < BF16_REL_L2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_zero_tokens(cuda, dtype):
+    """T = 0 (and B = 0): an empty output, and the state of zero tokens — the
+    input state unchanged, or zeros."""
+    from pulsartecture_b200.attention import TMLinKernelAttn, fa_kla
+    from pulsartecture_b200.backend.interface import fa_kla_attention_with_state
+    from pulsartecture_b200.kernels import LearnablePositiveMap
+
+    H, D = 2, 128
+    for B, T in ((2, 0), (0, 5)):
+        q = torch.rand(B, T, H, D, device=cuda).to(dtype)
+        out, (S, z) = fa_kla_attention_with_state(q, q, q, None, None, True)
+        assert out.shape == (B, T, H, D)
+        assert torch.count_nonzero(S) == 0 and torch.count_nonzero(z) == 0
+        S0 = torch.rand(B, H, D, D, device=cuda)
+        z0 = torch.rand(B, H, D, device=cuda)
+        _, (S1, z1) = fa_kla_attention_with_state(q, q, q, None, (S0, z0), True)
+        assert torch.equal(S1, S0) and torch.equal(z1, z0)
+        W, b = lpm_params(H * D, H * D, seed=3, dtype=dtype)
+        out2, (S2, z2) = fa_kla(q.reshape(B, T, H * D), q.reshape(B, T, H * D), q, phi_weight=W.to(cuda),
+                                phi_bias=b.to(cuda))
+        assert out2.shape == (B, T, H, D) and torch.count_nonzero(S2) == 0
+    mod = TMLinKernelAttn(H * D, LearnablePositiveMap(H * D, H * D, dtype=dtype), num_heads=H, qk_dim=D, v_dim=D,
+                          dtype=dtype).to(cuda).eval()
+    with torch.no_grad():
+        y = mod(torch.zeros(2, 0, H * D, device=cuda, dtype=dtype))
+    assert y.shape == (2, 0, H * D)
