@@ -21,6 +21,7 @@ arithmetic happens in libfakla.so.
 """
 from __future__ import annotations
 
+import threading
 from typing import Optional, Tuple
 
 import torch
@@ -328,11 +329,13 @@ class _HostPipeline:
 
 
 _HOST_PIPES: dict = {}
+_HOST_PIPES_LOCK = threading.Lock()  # one caller at a time queues work on a pipeline's slots
 
 
 def release_host_pipelines() -> None:
     """Free the device buffers fa_kla_prefill_host keeps between calls."""
-    _HOST_PIPES.clear()
+    with _HOST_PIPES_LOCK:
+        _HOST_PIPES.clear()
 
 
 def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
@@ -400,7 +403,7 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     ngroups = (B + mb - 1) // mb
     ns = min(slots, ngroups)
     ws_bytes = L.fakla_prefill_workspace_bytes(mb, T, in_dim, H, M, Dv, code)
-    with torch.cuda.device(dev):
+    with torch.cuda.device(dev), _HOST_PIPES_LOCK:
         main = torch.cuda.current_stream(dev)
         key = (mb, T, tuple(q.shape[2:]), H, Dv, dt, temp is not None, ws_bytes, ns)
         pipe = _HOST_PIPES.get(dev)
