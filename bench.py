@@ -379,6 +379,62 @@ def run_sustained(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- long context
+def run_longctx(args):
+    """Long-context prefill on one GPU: B=1, H=32, T=65536, Dk=Dv=M=128, bf16,
+    LearnablePositiveMap(4096 -> 4096) fused (fa_kla). The 32 sequences would
+    leave most SMs idle, so the scan runs segmented (segment sums, a prefix,
+    then one CTA per segment). Prints tokens/s, the phi GEMM and scan times
+    and the whole prefill's rate against the measured tensor peak."""
+    from pulsartecture_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    B_, T_, H_, D_ = 1, 65536, 32, 128
+    g = torch.Generator(device=dev).manual_seed(3)
+    q = (torch.randn(B_, T_, H_ * D_, generator=g, device=dev) / math.sqrt(D_)).bfloat16()
+    k = (torch.randn(B_, T_, H_ * D_, generator=g, device=dev) / math.sqrt(D_)).bfloat16()
+    v = (torch.randn(B_, T_, H_, D_, generator=g, device=dev) / math.sqrt(D_)).bfloat16()
+    W, bias = lpm_init(H_ * D_, H_ * D_)
+    W, bias = W.bfloat16().to(dev), bias.bfloat16().to(dev)
+    out = torch.empty_like(v)
+    S = torch.empty(B_, H_, D_, D_, device=dev)
+    z = torch.empty(B_, H_, D_, device=dev)
+    wsb = L.fakla_prefill_workspace_bytes(B_, T_, H_ * D_, H_, D_, D_, _lib.FAKLA_BF16)
+    ws = torch.empty(wsb, device=dev, dtype=torch.uint8)
+
+    def prefill():
+        _lib.check(L.fakla_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), None, W.data_ptr(), bias.data_ptr(),
+                                   out.data_ptr(), S.data_ptr(), z.data_ptr(), B_, T_, H_ * D_, H_, D_, D_,
+                                   _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, ws.data_ptr(), wsb, sh))
+
+    ph = torch.empty(2 * T_, H_ * D_, device=dev, dtype=torch.bfloat16)
+    xq = torch.cat([q.reshape(T_, -1), k.reshape(T_, -1)])
+
+    def phi():
+        _lib.check(L.fakla_phi(xq.data_ptr(), W.data_ptr(), bias.data_ptr(), None, ph.data_ptr(), 2 * T_,
+                               H_ * D_, H_ * D_, H_, _lib.FAKLA_BF16, sh))
+
+    res = {}
+    for name, fn in (("prefill", prefill), ("phi", phi)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        res[name] = time_loop(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+    _lib.check(L.fakla_device_status(sh))
+    _, tflops_burst, _, _ = peaks()
+    flops = 2 * (2 * T_) * (H_ * D_) * (H_ * D_) + T_ * H_ * 98304
+    line = {"only": "longctx", "workload": "FA-KLA prefill B=1, H=32, T=65536, Dk=Dv=M=128, bf16, phi 4096->4096 fused",
+            "ms": round(res["prefill"], 4), "tokens_per_s": round(T_ / res["prefill"] * 1e3, 1),
+            "phi_ms": round(res["phi"], 4), "scan_ms": round(res["prefill"] - res["phi"], 4),
+            "tflops": round(flops / res["prefill"] / 1e9, 1),
+            "frac_of_tensor_peak": round(flops / res["prefill"] / 1e9 / tflops_burst, 4)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- LM harness
 def run_lm(args):
     """Forward of the package's own end-to-end LM composition (lm_harness.py:
@@ -473,7 +529,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-module", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm"],
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -483,6 +539,8 @@ def main():
         return run_sustained(args)
     if args.only == "lm":
         return run_lm(args)
+    if args.only == "longctx":
+        return run_longctx(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
