@@ -224,7 +224,7 @@ typedef enum {
  *   out  : (rows, n_out), or (rows, 2 * n_out) for FAKLA_ACT_COSSIN: column n
  *          holds scale * cos(p_n) and column n_out + n holds scale * sin(p_n),
  *          p = x W^T + bias. `scale` is ignored by the other activations.
- * The tensor-core path serves BF16 with in_dim % 64 == 0, n_out % 256 == 0
+ * The tensor-core path serves BF16 with in_dim % 64 == 0, n_out % 128 == 0
  * and 16-byte aligned pointers; other shapes and F32 run on CUDA cores.
  */
 int fakla_feature_map(const void* x, const void* W, const void* bias, void* out,
@@ -287,7 +287,7 @@ size_t fakla_prefill_workspace_bytes(int64_t B, int64_t T, int64_t in_dim,
  *   temp : (B, T, H) or NULL     out : (B, T, H, Dv)
  *   S, z, flags : as fakla_attention, with Df = M.
  * Implemented for BF16 with M = Dv = 128 or 64, embed % 64 == 0, (2*H*M + H*Dv) %
- * 256 == 0, 16-byte aligned pointers; other cases return FAKLA_ERR_UNSUPPORTED.
+ * 128 == 0, 16-byte aligned pointers; other cases return FAKLA_ERR_UNSUPPORTED.
  * Workspace: fakla_qkv_prefill_workspace_bytes() (the GEMM output, then the
  * scan's optional segment records).
  */

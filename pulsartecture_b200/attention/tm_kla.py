@@ -152,7 +152,7 @@ class TMLinKernelAttn(nn.Module):
         dt = mapper.weight.dtype
         H, M, Dv = self.num_heads, self.feature_dim // self.num_heads, self.v_head_dim
         return (x.is_cuda and dt == torch.bfloat16 and M == Dv and M in (64, 128) and self.embed_dim % 64 == 0
-                and (2 * H * M + H * Dv) % 256 == 0 and self.feature_dim % self.num_heads == 0)
+                and (2 * H * M + H * Dv) % 128 == 0 and self.feature_dim % self.num_heads == 0)
 
     def _qkv_fold(self):
         """[Wphi Wq; Wphi Wk; Wv] and [Wphi bq + bphi; Wphi bk + bphi; bv], computed

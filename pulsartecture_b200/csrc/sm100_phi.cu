@@ -38,20 +38,21 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BN = 256;  // N tile; 128 (BNT below) when 256-wide tiles would not fill the GPU
 constexpr int BK = 64;
 constexpr int kStages = 4;
 constexpr int kABytes = BM * BK * 2;                 // 16 KB
-constexpr int kBBytes = BN * BK * 2;                 // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;       // 48 KB
+template <int BNT> constexpr int kBBytesT = BNT * BK * 2;             // 32 KB (BNT = 256)
+template <int BNT> constexpr int kStageBytesT = kABytes + kBBytesT<BNT>;  // 48 KB
 constexpr int kEpiWarps = 8;
 constexpr int kOutWarpBytes = 32 * 128;              // 32 rows x 64 bf16
 constexpr int kOutBytes = kEpiWarps * kOutWarpBytes;  // 32 KB (one buffer per warp)
 constexpr int kThreads = 64 + 32 * kEpiWarps;        // 320
-constexpr uint32_t kTmemCols = 2 * BN;               // 512
+template <int BNT> constexpr uint32_t kTmemColsT = 2 * BNT;  // 512 (BNT = 256)
 constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + (size_t)kStages * kStageBytes + kOutBytes + 256;
+template <int BNT>
+constexpr size_t kSmemBytesT = 1024 /*align slack*/ + (size_t)kStages * kStageBytesT<BNT> + kOutBytes + 256;
 
 struct PhiArgs {
   const __nv_bfloat16* bias;   // [N] or null
@@ -65,7 +66,7 @@ struct PhiArgs {
   int* status;
 };
 
-template <int ACT>
+template <int ACT, int BNT>
 __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC0,
@@ -75,6 +76,9 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;                                  // kStages x 16 KB
   uint8_t* sB = smem + kStages * kABytes;              // kStages x 32 KB
+  constexpr int kBBytes = kBBytesT<BNT>;
+  constexpr int kStageBytes = kStageBytesT<BNT>;
+  constexpr uint32_t kTmemCols = kTmemColsT<BNT>;
   uint8_t* sOut = sB + kStages * kBBytes;              // 32 KB (1024-aligned)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
   uint64_t* full = bars;                  // [kStages]
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   const int lane = threadIdx.x & 31;
 
   const int row_tiles = (args.rows + BM - 1) / BM;
-  const int col_tiles = args.N / BN;
+  const int col_tiles = args.N / BNT;
   const int tiles_per_set = row_tiles * col_tiles;
   const int total_tiles = tiles_per_set * args.nsets;
   const int kblocks = args.K / BK;
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         const int set = tile / tiles_per_set;
         const int r = tile % tiles_per_set;
         const int row0 = (r / col_tiles) * BM;
-        const int col0 = (r % col_tiles) * BN;
+        const int col0 = (r % col_tiles) * BNT;
         const CUtensorMap* mapA = set == 0 ? &tmA0 : &tmA1;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)) {
@@ -155,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BNT, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BNT);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, kWaitNs)) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
@@ -200,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;          // TMEM lane quadrant this warp may access
     const int ew = warp - 2;         // epilogue warp index (staging buffer owner)
-    const int half = ew >> 2;        // which 128 of the tile's 256 columns
+    const int half = ew >> 2;        // which half of the tile's BNT columns
+    constexpr int kWarpCols = BNT / 2;  // 128 or 64 columns per warp
     uint8_t* buf = sOut + ew * kOutWarpBytes;
     const int m = args.m;  // features per head
     int acc = 0;
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       const int set = tile / tiles_per_set;
       const int r = tile % tiles_per_set;
       const int row0 = (r / col_tiles) * BM;
-      const int col0 = (r % col_tiles) * BN + half * 128;
+      const int col0 = (r % col_tiles) * BNT + half * kWarpCols;
       const CUtensorMap* mapC = set == 0 ? &tmC0 : &tmC1;
       const __nv_bfloat16* temp = set == 0 ? args.temp0 : args.temp1;
       const int grow = row0 + 32 * q + lane;  // this thread's output row
@@ -221,14 +226,14 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       }
       tc_fence_after();
       const uint32_t t_row =
-          tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + half * 128);
+          tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BNT + half * kWarpCols);
 #pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kWarpCols / 64; ++j) {
         uint32_t v0[32], v1[32];
         tmem_ld32(t_row + (uint32_t)(j * 64), v0);
         tmem_ld32(t_row + (uint32_t)(j * 64 + 32), v1);
         tmem_ld_wait();
-        if (j == 1) {
+        if (j == kWarpCols / 64 - 1) {
           // this warp's share of the accumulator is in registers: release it
           tc_fence_before();
           __syncwarp();
@@ -331,24 +336,40 @@ static bool make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint
 }
 
 bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads) {
-  if (rows < 1 || K < BK || N < BN) return false;
-  if (K % BK != 0 || N % BN != 0) return false;
+  if (rows < 1 || K < BK || N < 128) return false;
+  if (K % BK != 0 || N % 128 != 0) return false;
   if (heads < 1 || N % heads != 0 || (N / heads) % 64 != 0) return false;
   if (rows > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX / 2 || N > (int64_t)INT32_MAX / 2)
     return false;
   return true;
 }
 
+template <int ACT, int BNT>
+static cudaError_t launch_act_t(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
+                                const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
+                                int grid, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel<ACT, BNT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytesT<BNT>);
+  if (e != cudaSuccess) return e;
+  phi_gemm_sm100_kernel<ACT, BNT><<<grid, kThreads, kSmemBytesT<BNT>, stream>>>(mA0, mA1, mB, mC0, mC1, a);
+  return cudaGetLastError();
+}
+
 template <int ACT>
 static cudaError_t launch_act(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
                               const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
-                              int grid, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel<ACT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
-  phi_gemm_sm100_kernel<ACT><<<grid, kThreads, kSmemBytes, stream>>>(mA0, mA1, mB, mC0, mC1, a);
-  return cudaGetLastError();
+                              int grid, int bn, cudaStream_t stream) {
+  return bn == 128 ? launch_act_t<ACT, 128>(mA0, mA1, mB, mC0, mC1, a, grid, stream)
+                   : launch_act_t<ACT, BN>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+}
+
+// The N tile: 256, or 128 when N is an odd multiple of 128 or when 256-wide
+// tiles would leave SMs idle (few rows, e.g. a decode step).
+static int pick_bn(int64_t rows, int64_t N, int nsets) {
+  const int64_t row_tiles = (rows + BM - 1) / BM;
+  if (N % BN != 0 || row_tiles * (N / BN) * nsets < fakla_sm_count()) return 128;
+  return BN;
 }
 
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
@@ -357,9 +378,10 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
                              float scale, cudaStream_t stream, int* status, bool* encoded) {
   CUtensorMap mA0, mA1, mB, mC0, mC1;
   const int nsets = x1 != nullptr ? 2 : 1;
+  const int bn = pick_bn(rows, N, nsets);
   const uint64_t out_cols = (uint64_t)N * (act == FAKLA_ACT_COSSIN ? 2 : 1);
   bool ok = make_map_2d(&mA0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, BN) &&
+            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)bn) &&
             make_map_2d(&mC0, out0, out_cols, (uint64_t)rows, 64, 32);
   if (ok && nsets == 2)
     ok = make_map_2d(&mA1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
@@ -386,24 +408,24 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   a.tcol1 = (int)N;
   a.status = status;
   const int row_tiles = (int)((rows + BM - 1) / BM);
-  const int total = row_tiles * (int)(N / BN) * nsets;
+  const int total = row_tiles * (int)(N / bn) * nsets;
   const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
   switch (act) {
-    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
-    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads) {
   const int64_t N = 2 * feat + vdim;
-  return rows >= 1 && K >= BK && K % BK == 0 && N % BN == 0 && feat % 64 == 0 && heads >= 1 &&
+  return rows >= 1 && K >= BK && K % BK == 0 && N % 128 == 0 && feat % 64 == 0 && heads >= 1 &&
          feat % heads == 0 && (feat / heads) % 64 == 0 && rows <= (int64_t)INT32_MAX &&
          K <= (int64_t)INT32_MAX / 2 && N <= (int64_t)INT32_MAX / 2;
 }
@@ -412,9 +434,10 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
                              void* out, int64_t rows, int64_t K, int64_t feat, int64_t vdim,
                              int64_t heads, cudaStream_t stream, int* status, bool* encoded) {
   const int64_t N = 2 * feat + vdim;
+  const int bn = pick_bn(rows, N, 1);
   CUtensorMap mA, mB, mC;
   const bool ok = make_map_2d(&mA, x, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, BN) &&
+                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)bn) &&
                   make_map_2d(&mC, out, (uint64_t)N, (uint64_t)rows, 64, 32);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
@@ -434,9 +457,9 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
   a.tcol1 = (int)(2 * feat);
   a.status = status;
   const int row_tiles = (int)((rows + BM - 1) / BM);
-  const int total = row_tiles * (int)(N / BN);
+  const int total = row_tiles * (int)(N / bn);
   const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
-  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, grid, stream);
+  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, grid, bn, stream);
 }
 
 }  // namespace fakla

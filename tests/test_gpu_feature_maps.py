@@ -38,7 +38,9 @@ def _inputs(rows, K, N, seed, dtype, dev, xscale=1.0):
 # ----------------------------------------------------------------- fakla_feature_map
 @pytest.mark.parametrize("act", ACTS)
 @pytest.mark.parametrize("rows,K,N,dtype", [
-    (1000, 256, 512, torch.bfloat16),    # tensor-core tiles
+    (1000, 256, 512, torch.bfloat16),    # tensor-core tiles (128 wide: 16 tiles of 256 would idle SMs)
+    (4000, 128, 1024, torch.bfloat16),   # tensor-core tiles 256 wide
+    (600, 192, 384, torch.bfloat16),     # tensor-core tiles, N an odd multiple of 128
     (77, 96, 40, torch.bfloat16),        # CUDA-core shape
     (300, 200, 96, torch.float32),       # fp32
 ])

@@ -232,13 +232,15 @@ def test_prefill_host_rejects_device_inputs(cuda):
 
 
 @pytest.mark.parametrize("T,with_temp,H,D", [(300, True, 4, 128), (1024, False, 4, 128),
-                                               (300, True, 8, 64), (777, False, 16, 64)])
+                                               (300, True, 8, 64), (777, False, 16, 64),
+                                               (500, True, 3, 128), (3000, False, 3, 128)])
 def test_module_qkv_folded_into_phi(cuda, T, with_temp, H, D):
     """Inference through fakla_qkv_prefill (projections folded into the feature
     map, one GEMM for [phi(q) | phi(k) temp | v]): equal to the projections,
     map and attention of the reference restated in float64 on the same bf16
     parameters, within the bf16 bars; the returned state too. Heads of 128 and
-    of 64."""
+    of 64; 3 heads of 128 give a [q|k|v] width of 1152, an odd multiple of 128
+    (128-wide GEMM tiles), at 6 and at 47 row tiles."""
     from pulsartecture_b200.attention import TMLinKernelAttn
     from pulsartecture_b200.kernels import LearnablePositiveMap
 
@@ -270,17 +272,17 @@ def test_module_qkv_folded_into_phi(cuda, T, with_temp, H, D):
 
 
 def test_module_qkv_fold_only_where_supported(cuda):
-    """The fold needs bf16, 128-wide heads and a 256-multiple GEMM width; other
-    modules keep the unfused path, and training keeps the autograd path."""
+    """The fold needs bf16 and heads of 64 or 128; other modules keep the
+    unfused path, and training keeps the autograd path."""
     from pulsartecture_b200.attention import TMLinKernelAttn
     from pulsartecture_b200.kernels import LearnablePositiveMap
 
     x = torch.zeros(1, 8, 384, dtype=torch.bfloat16, device=cuda)
-    mod = TMLinKernelAttn(384, LearnablePositiveMap(384, 384, dtype=torch.bfloat16), num_heads=3, qk_dim=128,
-                          v_dim=128, dtype=torch.bfloat16).to(cuda).eval()
-    assert not mod._qkv_foldable(x)  # 3 heads: the [q|k|v] width 1152 is not a multiple of 256
+    mod = TMLinKernelAttn(384, LearnablePositiveMap(288, 288, dtype=torch.bfloat16), num_heads=3, qk_dim=96,
+                          v_dim=96, dtype=torch.bfloat16).to(cuda).eval()
+    assert not mod._qkv_foldable(x)  # heads of 96
     with torch.no_grad():
-        assert mod(x).shape == (1, 8, 384)
+        assert mod(x).shape == (1, 8, 288)
     mod4 = TMLinKernelAttn(512, LearnablePositiveMap(512, 512, dtype=torch.bfloat16), num_heads=4, qk_dim=128,
                            v_dim=128, dtype=torch.bfloat16).to(cuda)
     x4 = torch.zeros(1, 8, 512, dtype=torch.bfloat16, device=cuda)
