@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """FA-KLA prefill benchmark (one JSON line on rank 0).
 
-Workload per GPU: FA-KLA prefill at B=8, H=16, T=4096, D=M=128, bf16 activations,
-fp32 state, causal, B=8, H=16, T=4096, Dk=Dv=M=128, feature map
+Workload per GPU: FA-KLA prefill at B=8, H=16, T=4096, Dk=Dv=M=128, bf16
+activations, fp32 state, causal, feature map
 LearnablePositiveMap(2048 -> 2048) fused (phi(q), phi(k), then the chunked
 scan); synthetic q, k, v ~ N(0,1)/sqrt(128) from a seed, map parameters
 initialised like the reference module from torch.manual_seed(0).
@@ -15,7 +15,8 @@ scaling, no collective on the data path); the step time is the max over
 ranks. `value` is all ranks' tokens / that time.
 
 Also reported: `e2e` (the same metric through the public API with pinned host
-buffers, host<->device copies inside the timed region), per-kernel times and
+buffers, host<->device copies inside the timed region; `e2e.link` times the
+same bytes copied alone, the PCIe floor of that step), per-kernel times and
 the roofline of the dominant kernel, the recurrent decode step (batch 256, H=32, D=128) in
 tokens/s and HBM GB/s, the CPU baseline (the reference's own CPU kernel,
 compiled from its sources into oracle/_ref, timed on a bounded sample on this
@@ -646,11 +647,37 @@ def main():
         ems = time_loop(e2e_step, e_steps, stream)
         sync_barrier(world)
         ems = max_over_ranks(ems, world, dev)
+        h2d_bytes, d2h_bytes = 3 * B * T * H * D * 2, B * T * H * D * 2
+
+        # the link floor of that step: the same bytes copied with no compute,
+        # inputs on one stream and the output on another (both directions at once)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        lq, lk, lv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        lout = torch.zeros(B, T, H, D, dtype=torch.bfloat16, device=dev)
+
+        def link_step():
+            s_in.wait_stream(stream)
+            s_out.wait_stream(stream)
+            with torch.cuda.stream(s_in):
+                for hsrc, ddst in ((hq, lq), (hk, lk), (hv, lv)):
+                    ddst.copy_(hsrc, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                hout.copy_(lout, non_blocking=True)
+            stream.wait_stream(s_in)
+            stream.wait_stream(s_out)
+
+        link_step()
+        lms = time_loop(link_step, e_steps, stream) / e_steps
+        del lq, lk, lv, lout
         e2e = {"value": B * T * world * e_steps / (ems / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": 3 * B * T * H * D * 2, "d2h_bytes_per_step": B * T * H * D * 2,
+               "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                "ms_per_step": ems / e_steps,
                "api": "pulsartecture_b200.attention.fa_kla_host (pinned host q/k/v in, host out; "
-                      "copies overlapped with compute per sequence and across steps, ordered=False)"}
+                      "copies overlapped with compute per sequence and across steps, ordered=False)",
+               "link": {"copies_only_ms_per_step": lms, "h2d_gbs": h2d_bytes / lms / 1e6,
+                        "frac": lms / (ems / e_steps),
+                        "note": "the step's host<->device bytes copied alone (pinned, both directions "
+                                "at once, no compute); frac = that time / the e2e step"}}
         del hq, hk, hv, hout
         from pulsartecture_b200.backend.interface import release_host_pipelines
         release_host_pipelines()
