@@ -23,6 +23,13 @@
 // sized to keep up with the tensor pipe: with it skipped the main loop was
 // measured at 98% of the bf16 peak, and a 4-warp epilogue with an accurate
 // exp cost 80% on top of that.
+//
+// Large GEMMs run the same kernel as CTA pairs (clusters of two): a pair
+// computes a 256x256 tile with cta_group::2 MMAs (256x256x16) issued by rank
+// 0; each CTA loads its 128 x rows and 128 of the tile's 256 W rows per stage
+// (6 stages of 32 KB), so each SM moves a third fewer operand bytes per FLOP
+// through L2 and shared memory. Rank 0's commits arrive on both CTAs'
+// barriers; each CTA runs the epilogue of its own 128 rows from its own TMEM.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -37,13 +44,16 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;
-constexpr int BN = 256;  // N tile; 128 (BNT below) when 256-wide tiles would not fill the GPU
+constexpr int BM = 128;   // rows of a tile per CTA
+constexpr int BN = 256;   // N tile; 128 (BNT below) when 256-wide tiles would not fill the GPU
 constexpr int BK = 64;
-constexpr int kStages = 4;
 constexpr int kABytes = BM * BK * 2;                 // 16 KB
-template <int BNT> constexpr int kBBytesT = BNT * BK * 2;             // 32 KB (BNT = 256)
-template <int BNT> constexpr int kStageBytesT = kABytes + kBBytesT<BNT>;  // 48 KB
+// Per CTA: a single CTA holds all BNT rows of the W tile; a CTA pair splits them.
+template <int BNT, bool PAIR> constexpr int kBRowsT = PAIR ? BNT / 2 : BNT;
+template <int BNT, bool PAIR> constexpr int kBBytesT = kBRowsT<BNT, PAIR> * BK * 2;
+template <int BNT, bool PAIR> constexpr int kStageBytesT = kABytes + kBBytesT<BNT, PAIR>;
+// 4 stages of 48 KB (single CTA, BNT 256) or 6 of 32 KB (pair, BNT 256)
+template <int BNT, bool PAIR> constexpr int kStagesT = PAIR ? 6 : 4;
 constexpr int kEpiWarps = 8;
 constexpr int kOutWarpBytes = 32 * 128;              // 32 rows x 64 bf16
 constexpr int kOutBytes = kEpiWarps * kOutWarpBytes;  // 32 KB (one buffer per warp)
@@ -51,8 +61,9 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;        // 320
 template <int BNT> constexpr uint32_t kTmemColsT = 2 * BNT;  // 512 (BNT = 256)
 constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
 
-template <int BNT>
-constexpr size_t kSmemBytesT = 1024 /*align slack*/ + (size_t)kStages * kStageBytesT<BNT> + kOutBytes + 256;
+template <int BNT, bool PAIR>
+constexpr size_t kSmemBytesT = 1024 /*align slack*/ +
+                               (size_t)kStagesT<BNT, PAIR> * kStageBytesT<BNT, PAIR> + kOutBytes + 256;
 
 struct PhiArgs {
   const __nv_bfloat16* bias;   // [N] or null
@@ -66,7 +77,11 @@ struct PhiArgs {
   int* status;
 };
 
-template <int ACT, int BNT>
+// PAIR: launched in clusters of two CTAs on neighbouring SMs that compute a
+// 256 x BNT tile together with cta_group::2 MMAs (rank 0 issues them; each
+// CTA loads its 128 rows of x and half of the W tile and runs the epilogue of
+// its 128 rows), so each SM streams a third fewer operand bytes per FLOP.
+template <int ACT, int BNT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC0,
@@ -74,11 +89,13 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sA = smem;                                  // kStages x 16 KB
-  uint8_t* sB = smem + kStages * kABytes;              // kStages x 32 KB
-  constexpr int kBBytes = kBBytesT<BNT>;
-  constexpr int kStageBytes = kStageBytesT<BNT>;
+  constexpr int kStages = kStagesT<BNT, PAIR>;
+  constexpr int kBBytes = kBBytesT<BNT, PAIR>;
+  constexpr int kStageBytes = kStageBytesT<BNT, PAIR>;
   constexpr uint32_t kTmemCols = kTmemColsT<BNT>;
+  constexpr int kTileRows = PAIR ? 2 * BM : BM;
+  uint8_t* sA = smem;                                  // kStages x 16 KB
+  uint8_t* sB = smem + kStages * kABytes;              // kStages x kBBytes
   uint8_t* sOut = sB + kStages * kBBytes;              // 32 KB (1024-aligned)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
   uint64_t* full = bars;                  // [kStages]
@@ -90,8 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0 issues the MMAs
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
-  const int row_tiles = (args.rows + BM - 1) / BM;
+  const int row_tiles = (args.rows + kTileRows - 1) / kTileRows;
   const int col_tiles = args.N / BNT;
   const int tiles_per_set = row_tiles * col_tiles;
   const int total_tiles = tiles_per_set * args.nsets;
@@ -104,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -115,57 +135,81 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     tma_prefetch_desc(&tmC1);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair's barriers must be initialised before the other CTA signals them
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Single CTA: waits for a free stage, loads the x tile and the W tile.
+    // Pair: each CTA loads its 128 x rows and its half of the W tile into its
+    // own stage, counted against rank 0's `full` barrier; rank 0's MMA
+    // commits release the stage in both CTAs' `empty` barriers.
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       long it = 0;
-      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
         const int set = tile / tiles_per_set;
         const int r = tile % tiles_per_set;
-        const int row0 = (r / col_tiles) * BM;
-        const int col0 = (r % col_tiles) * BNT;
+        const int row0 = (r / col_tiles) * kTileRows + (int)rank * BM;
+        const int col0 = (r % col_tiles) * BNT + (int)rank * kBRowsT<BNT, PAIR>;
         const CUtensorMap* mapA = set == 0 ? &tmA0 : &tmA1;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)) {
+          const bool free = rank == 0 ? mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)
+                                      : mbar_wait_cluster(&empty[stage], phase ^ 1u, kWaitNs);
+          if (!free) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sA + stage * kABytes, mapA, &full[stage], kb * BK, row0);
-          tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * BK, col0);
+          if constexpr (PAIR) {
+            const uint32_t fb = mapa_shared(&full[stage], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+            tma_load_2d_pair(sA + stage * kABytes, mapA, fb, kb * BK, row0);
+            tma_load_2d_pair(sB + stage * kBBytes, &tmB, fb, kb * BK, col0);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(sA + stage * kABytes, mapA, &full[stage], kb * BK, row0);
+            tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * BK, col0);
+          }
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (*abort_flag) {
-        // Let this CTA's copies in flight land before it exits.
+      if (*abort_flag && rank == 0) {
+        // Let the copies in flight land before the CTA exits (rank 1's
+        // copies count against rank 0's barriers, which it cannot wait on;
+        // the cluster barrier at the end holds it until rank 0 is done).
         for (long i = it - kStages; i < it; ++i)
           if (i >= 0) (void)mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u, kWaitNs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BNT, false, false);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kTileRows, BNT, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, kWaitNs)) {
+      for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
+        const bool drained = PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, kWaitNs)
+                                  : mbar_wait(&tempty[acc], acc_phase ^ 1u, kWaitNs);
+        if (!drained) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
           break;
@@ -184,16 +228,26 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // advance 16 bf16 = 32 bytes along K inside the 128-byte swizzle atom
-            mma_ss(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                   (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              mma_ss_pair(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                          (kb | k) != 0 ? 1u : 0u);
+            else
+              mma_ss(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                     (kb | k) != 0 ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          if constexpr (PAIR)
+            mma_commit_pair(&empty[stage]);
+          else
+            mma_commit(&empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        mma_commit(&tfull[acc]);
+        if constexpr (PAIR)
+          mma_commit_pair(&tfull[acc]);
+        else
+          mma_commit(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -211,15 +265,18 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     int acc = 0;
     uint32_t acc_phase = 0;
     bool stored = false;
-    for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+    for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
       const int set = tile / tiles_per_set;
       const int r = tile % tiles_per_set;
-      const int row0 = (r / col_tiles) * BM;
+      const int row0 = (r / col_tiles) * kTileRows + (int)rank * BM;  // this CTA's 128 rows
       const int col0 = (r % col_tiles) * BNT + half * kWarpCols;
       const CUtensorMap* mapC = set == 0 ? &tmC0 : &tmC1;
       const __nv_bfloat16* temp = set == 0 ? args.temp0 : args.temp1;
       const int grow = row0 + 32 * q + lane;  // this thread's output row
-      if (!mbar_wait(&tfull[acc], acc_phase, kWaitNs)) {
+      // Pair: rank 0's commit lands on both CTAs' `tfull`.
+      const bool ready = rank == 0 ? mbar_wait(&tfull[acc], acc_phase, kWaitNs)
+                                   : mbar_wait_cluster(&tfull[acc], acc_phase, kWaitNs);
+      if (!ready) {
         report_status(args.status, FAKLA_ERR_TIMEOUT);
         *abort_flag = 1;
         break;
@@ -237,7 +294,12 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           // this warp's share of the accumulator is in registers: release it
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (lane == 0) {
+            if (rank == 0)
+              mbar_arrive(&tempty[acc]);
+            else
+              mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+          }
         }
         const int c0 = col0 + j * 64;
         const bool ident = c0 >= args.ident_from;  // identity columns (the v block of a q/k/v GEMM)
@@ -297,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
+          if (lane == 0 && row0 + 32 * q < args.rows) {
             tma_store_2d(mapC, buf, c0 + pass * args.N, row0 + 32 * q);
             bulk_commit_group();
           }
@@ -314,9 +376,15 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
 
   tc_fence_before();
   __syncthreads();
+  // a pair's CTAs exit together: rank 0's MMAs read rank 1's shared memory and
+  // write its TMEM, and rank 1 arrives on rank 0's barriers
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -344,32 +412,106 @@ bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads) {
   return true;
 }
 
-template <int ACT, int BNT>
-static cudaError_t launch_act_t(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
-                                const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
-                                int grid, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(phi_gemm_sm100_kernel<ACT, BNT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytesT<BNT>);
-  if (e != cudaSuccess) return e;
-  phi_gemm_sm100_kernel<ACT, BNT><<<grid, kThreads, kSmemBytesT<BNT>, stream>>>(mA0, mA1, mB, mC0, mC1, a);
-  return cudaGetLastError();
+// Tile shapes: 0 = single CTA, 128 x 256; 1 = single CTA, 128 x 128;
+// 2 = CTA pair, 256 x 256.
+enum PhiTiling { kTile256 = 0, kTile128 = 1, kTilePair = 2 };
+
+// Pairs of CTAs that can be resident at once (a pair needs two SMs of one
+// GPC), per device; 0 if the query failed.
+static int pair_slots() {
+  static int cached[64];
+  static bool done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!done[dev]) {
+    int n = 0;
+    const auto kern = phi_gemm_sm100_kernel<FAKLA_ACT_ELU1, BN, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kSmemBytesT<BN, true>) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * fakla_sm_count());
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmemBytesT<BN, true>;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    (void)cudaGetLastError();
+    cached[dev] = n;
+    done[dev] = true;
+  }
+  return cached[dev];
 }
 
+// CTA pairs when N allows 256-wide tiles and there are enough 256 x 256
+// tiles to occupy every pair; otherwise single CTAs with 256-wide tiles, or
+// 128-wide ones when N is an odd multiple of 128 or when 256-wide tiles would
+// leave SMs idle (few rows, e.g. a decode step).
+static int pick_tiling(int64_t rows, int64_t N, int nsets) {
+  if (N % BN == 0) {
+    const int slots = pair_slots();
+    if (slots > 0 && ((rows + 2 * BM - 1) / (2 * BM)) * (N / BN) * nsets >= slots) return kTilePair;
+  }
+  const int64_t row_tiles = (rows + BM - 1) / BM;
+  if (N % BN != 0 || row_tiles * (N / BN) * nsets < fakla_sm_count()) return kTile128;
+  return kTile256;
+}
+
+static int tiling_bn(int tiling) { return tiling == kTile128 ? 128 : BN; }
+// rows of W per CTA per stage (the TMA box height of the W map)
+static int tiling_b_rows(int tiling) { return tiling == kTilePair ? BN / 2 : tiling_bn(tiling); }
+
+template <int ACT, int BNT, bool PAIR>
+static cudaError_t launch_act_t(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
+                                const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
+                                int64_t tiles, cudaStream_t stream) {
+  const auto kern = phi_gemm_sm100_kernel<ACT, BNT, PAIR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytesT<BNT, PAIR>);
+  if (e != cudaSuccess) return e;
+  if constexpr (PAIR) {
+    const int64_t pairs = tiles < pair_slots() ? tiles : pair_slots();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytesT<BNT, PAIR>;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, mA0, mA1, mB, mC0, mC1, a);
+  } else {
+    const int sms = fakla_sm_count();
+    const int grid = tiles < sms ? (int)tiles : sms;
+    kern<<<grid, kThreads, kSmemBytesT<BNT, PAIR>, stream>>>(mA0, mA1, mB, mC0, mC1, a);
+    return cudaGetLastError();
+  }
+}
+
+// `tiles`: the number of output tiles of the chosen shape (all row sets).
 template <int ACT>
 static cudaError_t launch_act(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
                               const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
-                              int grid, int bn, cudaStream_t stream) {
-  return bn == 128 ? launch_act_t<ACT, 128>(mA0, mA1, mB, mC0, mC1, a, grid, stream)
-                   : launch_act_t<ACT, BN>(mA0, mA1, mB, mC0, mC1, a, grid, stream);
+                              int64_t tiles, int tiling, cudaStream_t stream) {
+  switch (tiling) {
+    case kTilePair: return launch_act_t<ACT, BN, true>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
+    case kTile128: return launch_act_t<ACT, 128, false>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
+    default: return launch_act_t<ACT, BN, false>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
+  }
 }
 
-// The N tile: 256, or 128 when N is an odd multiple of 128 or when 256-wide
-// tiles would leave SMs idle (few rows, e.g. a decode step).
-static int pick_bn(int64_t rows, int64_t N, int nsets) {
-  const int64_t row_tiles = (rows + BM - 1) / BM;
-  if (N % BN != 0 || row_tiles * (N / BN) * nsets < fakla_sm_count()) return 128;
-  return BN;
+static int64_t tile_count(int64_t rows, int64_t N, int nsets, int tiling) {
+  const int64_t tile_rows = tiling == kTilePair ? 2 * BM : BM;
+  return ((rows + tile_rows - 1) / tile_rows) * (N / tiling_bn(tiling)) * nsets;
 }
 
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
@@ -378,10 +520,10 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
                              float scale, cudaStream_t stream, int* status, bool* encoded) {
   CUtensorMap mA0, mA1, mB, mC0, mC1;
   const int nsets = x1 != nullptr ? 2 : 1;
-  const int bn = pick_bn(rows, N, nsets);
+  const int tiling = pick_tiling(rows, N, nsets);
   const uint64_t out_cols = (uint64_t)N * (act == FAKLA_ACT_COSSIN ? 2 : 1);
   bool ok = make_map_2d(&mA0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)bn) &&
+            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)tiling_b_rows(tiling)) &&
             make_map_2d(&mC0, out0, out_cols, (uint64_t)rows, 64, 32);
   if (ok && nsets == 2)
     ok = make_map_2d(&mA1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
@@ -407,18 +549,16 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   a.tcol0 = 0;
   a.tcol1 = (int)N;
   a.status = status;
-  const int row_tiles = (int)((rows + BM - 1) / BM);
-  const int total = row_tiles * (int)(N / bn) * nsets;
-  const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
+  const int64_t tiles = tile_count(rows, N, nsets, tiling);
   switch (act) {
-    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
-    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, grid, bn, stream);
+    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -434,10 +574,10 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
                              void* out, int64_t rows, int64_t K, int64_t feat, int64_t vdim,
                              int64_t heads, cudaStream_t stream, int* status, bool* encoded) {
   const int64_t N = 2 * feat + vdim;
-  const int bn = pick_bn(rows, N, 1);
+  const int tiling = pick_tiling(rows, N, 1);
   CUtensorMap mA, mB, mC;
   const bool ok = make_map_2d(&mA, x, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)bn) &&
+                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)tiling_b_rows(tiling)) &&
                   make_map_2d(&mC, out, (uint64_t)N, (uint64_t)rows, 64, 32);
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
@@ -456,10 +596,7 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
   a.tcol0 = (int)feat;
   a.tcol1 = (int)(2 * feat);
   a.status = status;
-  const int row_tiles = (int)((rows + BM - 1) / BM);
-  const int total = row_tiles * (int)(N / bn);
-  const int grid = total < fakla_sm_count() ? total : fakla_sm_count();
-  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, grid, bn, stream);
+  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, tile_count(rows, N, 1, tiling), tiling, stream);
 }
 
 }  // namespace fakla

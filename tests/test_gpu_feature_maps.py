@@ -41,6 +41,8 @@ def _inputs(rows, K, N, seed, dtype, dev, xscale=1.0):
     (1000, 256, 512, torch.bfloat16),    # tensor-core tiles (128 wide: 16 tiles of 256 would idle SMs)
     (4000, 128, 1024, torch.bfloat16),   # tensor-core tiles 256 wide
     (600, 192, 384, torch.bfloat16),     # tensor-core tiles, N an odd multiple of 128
+    (20000, 128, 1024, torch.bfloat16),  # CTA-pair 256x256 tiles (316 of them)
+    (19999, 192, 512, torch.bfloat16),   # CTA-pair tiles, last one ragged (rank 1 partly past the end)
     (77, 96, 40, torch.bfloat16),        # CUDA-core shape
     (300, 200, 96, torch.float32),       # fp32
 ])
@@ -58,6 +60,7 @@ def test_feature_map_activations(cuda, act, rows, K, N, dtype):
 
 @pytest.mark.parametrize("rows,K,P,dtype", [
     (1000, 256, 256, torch.bfloat16),    # tensor cores, cos/sin epilogue
+    (19001, 128, 512, torch.bfloat16),   # CTA-pair tiles, cos/sin epilogue
     (50, 64, 40, torch.bfloat16),
     (300, 200, 96, torch.float32),
 ])
