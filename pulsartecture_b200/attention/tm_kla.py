@@ -269,7 +269,7 @@ def fa_kla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[St
 def fa_kla_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[State] = None, *,
                 phi_weight: torch.Tensor, phi_bias: Optional[torch.Tensor] = None,
                 temp: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                micro_batch: int = 1, ordered: bool = True) -> Tuple[torch.Tensor, State]:
+                micro_batch: Optional[int] = None, ordered: bool = True) -> Tuple[torch.Tensor, State]:
     """``fa_kla`` for inputs that live in host memory: q, k, v (and temp) on the
     CPU, phi_weight/phi_bias on the GPU that runs the call; returns the output
     in host memory and the state on the GPU. Transfers in both directions

@@ -341,7 +341,7 @@ def release_host_pipelines() -> None:
 def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
                         bias: Optional[torch.Tensor] = None, temp: Optional[torch.Tensor] = None,
                         state: Optional[State] = None, return_state: bool = True,
-                        out: Optional[torch.Tensor] = None, micro_batch: int = 1, slots: int = 3,
+                        out: Optional[torch.Tensor] = None, micro_batch: Optional[int] = None, slots: int = 3,
                         ordered: bool = True):
     """phi fused with FA-KLA on HOST tensors, transfers overlapped with compute.
 
@@ -352,7 +352,10 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     of ``micro_batch`` sequences that flow through ``slots`` device buffers:
     the host->device copy of one group, the fused prefill of the previous one
     and the device->host copy of the one before run on three streams at once
-    (the two copy directions use separate copy engines).
+    (the two copy directions use separate copy engines). By default a group
+    holds enough sequences for its q copy to reach 64 MiB, and at most half
+    the batch: fewer, larger copies keep the link busier (B=8, T=4096,
+    in_dim=2048 bf16: groups of 4 ran 3 % faster than single sequences).
 
     Returns (out, state): ``out`` is a (B, T, H, Dv) host tensor (pinned unless
     given), state (S, z) on the GPU. Like a ``non_blocking`` copy, the call
@@ -388,6 +391,9 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
     dt = q.dtype
     _require(all(t is None or t.dtype == dt for t in (k, v, weight, bias, temp)), "All inputs must have the same dtype")
     _require(all(t is None or t.is_contiguous() for t in (q, k, v, weight, bias, temp)), "All inputs must be contiguous")
+    if micro_batch is None:
+        per_seq = max(1, T * in_dim * q.element_size())
+        micro_batch = max(1, min(max(1, B // 2), -(-(64 << 20) // per_seq)))
     _require(micro_batch >= 1 and slots >= 2, "micro_batch >= 1 and slots >= 2")
     code = _dtype_code(q)
     _check_state(state, B, H, M, Dv, dev)

@@ -160,10 +160,11 @@ def test_native_library_is_loaded(cuda):
     assert "libfakla.so" in maps
 
 
-@pytest.mark.parametrize("micro_batch", [1, 2])
+@pytest.mark.parametrize("micro_batch", [1, 2, None])
 def test_prefill_host_streaming_matches_device_and_oracle(cuda, micro_batch):
     """fa_kla_host: host q/k/v/temp in, host out, copies overlapped with compute
-    over groups of sequences (the last group ragged); same results as the
+    over groups of sequences (the last group ragged; None: the default size,
+    here one sequence, half of the batch rounded down); same results as the
     device call and the oracle, initial state carried per sequence."""
     from pulsartecture_b200.attention import fa_kla, fa_kla_host
 
@@ -233,14 +234,16 @@ def test_prefill_host_rejects_device_inputs(cuda):
 
 @pytest.mark.parametrize("T,with_temp,H,D", [(300, True, 4, 128), (1024, False, 4, 128),
                                                (300, True, 8, 64), (777, False, 16, 64),
-                                               (500, True, 3, 128), (3000, False, 3, 128)])
+                                               (500, True, 3, 128), (3000, False, 3, 128),
+                                               (4096, True, 4, 128)])
 def test_module_qkv_folded_into_phi(cuda, T, with_temp, H, D):
     """Inference through fakla_qkv_prefill (projections folded into the feature
     map, one GEMM for [phi(q) | phi(k) temp | v]): equal to the projections,
     map and attention of the reference restated in float64 on the same bf16
     parameters, within the bf16 bars; the returned state too. Heads of 128 and
     of 64; 3 heads of 128 give a [q|k|v] width of 1152, an odd multiple of 128
-    (128-wide GEMM tiles), at 6 and at 47 row tiles."""
+    (128-wide GEMM tiles), at 6 and at 47 row tiles; 2 x 4096 tokens of 4 heads
+    of 128 run the GEMM as CTA pairs (192 tiles of 256 x 256)."""
     from pulsartecture_b200.attention import TMLinKernelAttn
     from pulsartecture_b200.kernels import LearnablePositiveMap
 
