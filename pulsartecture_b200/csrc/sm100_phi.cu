@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   uint64_t* empty = bars + kStages;       // [kStages]
   uint64_t* tfull = bars + 2 * kStages;   // [2]
   uint64_t* tempty = tfull + 2;           // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;           // [1] MMAs in flight after an abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -126,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA0);
@@ -252,6 +254,15 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           acc = 0;
           acc_phase ^= 1u;
         }
+      }
+      if (*abort_flag) {
+        // Let the MMAs already issued finish before TMEM is freed (and, for a
+        // pair, before the other CTA's shared memory goes away).
+        if constexpr (PAIR)
+          mma_commit_pair(drain);
+        else
+          mma_commit(drain);
+        (void)mbar_wait(drain, 0u, kWaitNs);
       }
     }
   } else {
