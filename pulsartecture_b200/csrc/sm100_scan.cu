@@ -306,13 +306,14 @@ __device__ __forceinline__ void put_sb8(uint8_t* sb, uint8_t* sb_lo, int r, int 
 __device__ __forceinline__ void stage_scaled_32(const uint32_t (&v)[32], float inv, uint8_t* tile,
                                                 int r, int col0) {
   uint8_t* atom = tile + (col0 >= 64 ? kAtom : 0);
+  const uint64_t inv2 = f2_splat(inv);
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     uint4 u;
-    u.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * inv, __uint_as_float(v[8 * g + 1]) * inv);
-    u.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * inv, __uint_as_float(v[8 * g + 3]) * inv);
-    u.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * inv, __uint_as_float(v[8 * g + 5]) * inv);
-    u.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * inv, __uint_as_float(v[8 * g + 7]) * inv);
+    u.x = pack_bf16x2(f2_mul(f2_make(v[8 * g + 0], v[8 * g + 1]), inv2));
+    u.y = pack_bf16x2(f2_mul(f2_make(v[8 * g + 2], v[8 * g + 3]), inv2));
+    u.z = pack_bf16x2(f2_mul(f2_make(v[8 * g + 4], v[8 * g + 5]), inv2));
+    u.w = pack_bf16x2(f2_mul(f2_make(v[8 * g + 6], v[8 * g + 7]), inv2));
     *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((col0 & 63) + 8 * g))) = u;
   }
 }
@@ -363,44 +364,50 @@ __device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv,
 // mv only with kM) are read as broadcasts. With kDot the return value is
 // sum(x + coef * vec + sig * mv) * k over these columns, k = 32 bf16 of this
 // row (4 uint4), else 0.
+// Columns are processed as fp32 pairs on the paired FP32 pipe (each element
+// rounded as the scalar fmaf/multiply would round it); the dot keeps the
+// even and odd columns in the two halves of one accumulator pair.
 template <bool kDot, bool kM>
 __device__ __forceinline__ float stage_affine_32(const uint32_t (&v)[32], float coef, const float* vec,
                                                  float sig, const float* mv, float scale,
                                                  const uint4* krow, uint8_t* tile, int r, int col0) {
   uint8_t* atom = tile + (col0 >= 64 ? kAtom : 0);
-  float dot0 = 0.f, dot1 = 0.f;
+  const uint64_t coef2 = f2_splat(coef), sig2 = f2_splat(sig), scale2 = f2_splat(scale);
+  const bool scaled = scale != 1.f;  // multiplying by 1 changes nothing
+  uint64_t dot2 = f2_splat(0.f);
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const float4 w0 = reinterpret_cast<const float4*>(vec)[2 * g];
-    const float4 w1 = reinterpret_cast<const float4*>(vec)[2 * g + 1];
-    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    float y[8];
+    const ulonglong2 w01 = reinterpret_cast<const ulonglong2*>(vec)[2 * g];
+    const ulonglong2 w23 = reinterpret_cast<const ulonglong2*>(vec)[2 * g + 1];
+    const uint64_t w[4] = {w01.x, w01.y, w23.x, w23.y};
+    uint64_t y[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = fmaf(coef, w[e], __uint_as_float(v[8 * g + e]));
+    for (int e = 0; e < 4; ++e) y[e] = f2_fma(coef2, w[e], f2_make(v[8 * g + 2 * e], v[8 * g + 2 * e + 1]));
     if (kM) {
-      const float4 m0 = reinterpret_cast<const float4*>(mv)[2 * g];
-      const float4 m1 = reinterpret_cast<const float4*>(mv)[2 * g + 1];
-      const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      const ulonglong2 m01 = reinterpret_cast<const ulonglong2*>(mv)[2 * g];
+      const ulonglong2 m23 = reinterpret_cast<const ulonglong2*>(mv)[2 * g + 1];
+      const uint64_t m[4] = {m01.x, m01.y, m23.x, m23.y};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = fmaf(sig, m[e], y[e]);
+      for (int e = 0; e < 4; ++e) y[e] = f2_fma(sig2, m[e], y[e]);
     }
     if (kDot) {
-      float kf[8];
-      bf16x8_to_f32(krow[g], kf);
+      const uint32_t kw[4] = {krow[g].x, krow[g].y, krow[g].z, krow[g].w};
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        dot0 = fmaf(y[e], kf[e], dot0);
-        dot1 = fmaf(y[e + 1], kf[e + 1], dot1);
-      }
+      for (int e = 0; e < 4; ++e) dot2 = f2_fma(y[e], f2_make(kw[e] << 16, kw[e] & 0xffff0000u), dot2);
+    }
+    if (scaled) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = f2_mul(y[e], scale2);
     }
     uint4 u;
-    u.x = pack_bf16x2(y[0] * scale, y[1] * scale);
-    u.y = pack_bf16x2(y[2] * scale, y[3] * scale);
-    u.z = pack_bf16x2(y[4] * scale, y[5] * scale);
-    u.w = pack_bf16x2(y[6] * scale, y[7] * scale);
+    u.x = pack_bf16x2(y[0]);
+    u.y = pack_bf16x2(y[1]);
+    u.z = pack_bf16x2(y[2]);
+    u.w = pack_bf16x2(y[3]);
     *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((col0 & 63) + 8 * g))) = u;
   }
-  return dot0 + dot1;
+  const float2 d = f2_split(dot2);
+  return d.x + d.y;
 }
 
 // Warp-uniform forms of the bounded wait and of the abort check, for warps

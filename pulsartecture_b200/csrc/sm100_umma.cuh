@@ -16,6 +16,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -448,9 +449,39 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-  const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-  return l | (h << 16);
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);  // one cvt.rn.bf16x2.f32
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// ----------------------------------------------------------------- f32x2
+// Packed pairs of fp32 (element 0 in the low word) for the sm_100 paired
+// FP32 pipe: each lane is rounded exactly like the scalar operation.
+__device__ __forceinline__ uint64_t f2_make(uint32_t lo_bits, uint32_t hi_bits) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo_bits), "r"(hi_bits));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_splat(float x) {
+  return f2_make(__float_as_uint(x), __float_as_uint(x));
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v) {
+  const float2 f = f2_split(v);
+  return pack_bf16x2(f.x, f.y);
 }
 
 }  // namespace sm100
