@@ -231,31 +231,28 @@ __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase,
                                              uint32_t p_addr, float arow, const float* bcol) {
   uint32_t hi[16], lo[16];
   float rs = 0.f;
+  const uint64_t arow2 = f2_splat(arow);
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    float x0 = __uint_as_float(v[2 * e]), x1 = __uint_as_float(v[2 * e + 1]);
-    if (kRow) {  // (x + 0 is not folded away: keep the add out of the other modes)
-      x0 += arow;
-      x1 += arow;
+    // token pair (2e, 2e+1) as an fp32 pair on the paired FP32 pipe
+    uint64_t x = f2_make(v[2 * e], v[2 * e + 1]);
+    if (kRow) x = f2_add(x, arow2);  // (x + 0 is not folded away: keep the add out of the other modes)
+    if (kCol) x = f2_add(x, reinterpret_cast<const uint64_t*>(bcol)[e]);
+    if (kMask != 0) {
+      float2 xf = f2_split(x);
+      if (kMask == 1) {
+        xf.x = sbase + 2 * e <= r ? xf.x : 0.f;
+        xf.y = sbase + 2 * e + 1 <= r ? xf.y : 0.f;
+      } else {
+        xf.x = sbase + 2 * e >= r ? xf.x : 0.f;
+        xf.y = sbase + 2 * e + 1 >= r ? xf.y : 0.f;
+      }
+      x = f2_make(__float_as_uint(xf.x), __float_as_uint(xf.y));
     }
-    if (kCol) {
-      const float2 bb = reinterpret_cast<const float2*>(bcol)[e];
-      x0 += bb.x;
-      x1 += bb.y;
-    }
-    if (kMask == 1) {
-      x0 = sbase + 2 * e <= r ? x0 : 0.f;
-      x1 = sbase + 2 * e + 1 <= r ? x1 : 0.f;
-    } else if (kMask == 2) {
-      x0 = sbase + 2 * e >= r ? x0 : 0.f;
-      x1 = sbase + 2 * e + 1 >= r ? x1 : 0.f;
-    }
-    rs += x0 + x1;
-    const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-    const float2 hf = __bfloat1622float2(h2);
-    const __nv_bfloat162 l2 = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
-    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-    lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
+    const float2 xf = f2_split(x);
+    rs += xf.x + xf.y;
+    hi[e] = pack_bf16x2(xf.x, xf.y);
+    lo[e] = pack_bf16x2(f2_sub(x, f2_from_bf16x2(hi[e])));
   }
   tmem_st16(p_addr + (uint32_t)sbase, hi);
   tmem_st16(p_addr + (uint32_t)(sbase + 16), lo);
@@ -340,22 +337,19 @@ __device__ __forceinline__ void store_row_smem(uint8_t* tile, int r, int c0, con
 // in v), g = 32 bf16 of the output gradient row (4 uint4). g is replaced by
 // bf16(g * inv) (dnum, rounded as bf16 pairs), the value the sum uses.
 __device__ __forceinline__ float dden_dot_32(const uint32_t (&v)[32], float inv, uint4* g) {
-  float acc0 = 0.f, acc1 = 0.f;
+  const uint64_t inv2 = f2_splat(inv);
+  uint64_t acc = f2_splat(0.f);  // even columns in the low half, odd in the high half
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    float gf[8];
-    bf16x8_to_f32(g[k], gf);
     uint32_t* w = reinterpret_cast<uint32_t*>(&g[k]);
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const __nv_bfloat162 d2 = __floats2bfloat162_rn(gf[e] * inv, gf[e + 1] * inv);
-      w[e / 2] = *reinterpret_cast<const uint32_t*>(&d2);
-      const float2 dn = __bfloat1622float2(d2);
-      acc0 = fmaf(dn.x, __uint_as_float(v[8 * k + e]), acc0);
-      acc1 = fmaf(dn.y, __uint_as_float(v[8 * k + e + 1]), acc1);
+    for (int e = 0; e < 4; ++e) {
+      w[e] = pack_bf16x2(f2_mul(f2_from_bf16x2(w[e]), inv2));
+      acc = f2_fma(f2_from_bf16x2(w[e]), f2_make(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]), acc);
     }
   }
-  return (acc0 + acc1) * inv;
+  const float2 a = f2_split(acc);
+  return (a.x + a.y) * inv;
 }
 
 // Backward epilogue of one row: y = (x + coef * vec + sig * mv) * scale over
