@@ -285,13 +285,10 @@ __device__ __forceinline__ void put_sb8(uint8_t* sb, uint8_t* sb_lo, int r, int 
   uint32_t hi[4], lo[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
-    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-    if (kLo) {
-      const float2 hf = __bfloat1622float2(h2);
-      const __nv_bfloat162 l2 = __floats2bfloat162_rn(f[2 * e] - hf.x, f[2 * e + 1] - hf.y);
-      lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
-    }
+    hi[e] = pack_bf16x2(f[2 * e], f[2 * e + 1]);
+    if (kLo)
+      lo[e] = pack_bf16x2(f2_sub(f2_make(__float_as_uint(f[2 * e]), __float_as_uint(f[2 * e + 1])),
+                                 f2_from_bf16x2(hi[e])));
   }
   const uint32_t off = (c >= 64 ? kAtom : 0) + sw128_offset((uint32_t)r, (uint32_t)(c & 63));
   *reinterpret_cast<uint4*>(sb + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
