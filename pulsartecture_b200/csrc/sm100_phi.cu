@@ -35,6 +35,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "fakla_common.cuh"
 #include "fakla_kernels.h"
 #include "sm100_umma.cuh"
@@ -341,22 +343,33 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
 #pragma unroll 1
         for (int pass = 0; pass < kPasses; ++pass) {
           uint32_t packed[32];
+          const uint64_t tscale2 = f2_splat(tscale);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const uint32_t raw_a = i < 16 ? v0[2 * i] : v1[2 * i - 32];
             const uint32_t raw_b = i < 16 ? v0[2 * i + 1] : v1[2 * i + 1 - 32];
-            const float a = __uint_as_float(raw_a) + __uint_as_float(bw[i] << 16);
-            const float b = __uint_as_float(raw_b) + __uint_as_float(bw[i] & 0xffff0000u);
+            // columns 2i, 2i+1 as an fp32 pair (paired FP32 pipe; each lane
+            // rounds as the scalar operation would)
+            const uint64_t x = f2_add(f2_make(raw_a, raw_b), f2_from_bf16x2(bw[i]));
+            const float2 ab = f2_split(x);
+            const float a = ab.x, b = ab.y;
             if constexpr (ACT == FAKLA_ACT_COSSIN) {
               const float fa = pass == 0 ? cosf(a) : sinf(a);
               const float fb = pass == 0 ? cosf(b) : sinf(b);
               packed[i] = pack_bf16x2(fa * args.scale * tscale, fb * args.scale * tscale);
             } else if (ident) {
-              packed[i] = pack_bf16x2(a, b);
-            } else if (scaled) {
-              packed[i] = pack_bf16x2(activate<ACT, true>(a) * tscale, activate<ACT, true>(b) * tscale);
+              packed[i] = pack_bf16x2(x);
             } else {
-              packed[i] = pack_bf16x2(activate<ACT, true>(a), activate<ACT, true>(b));
+              uint64_t y;
+              if constexpr (ACT == FAKLA_ACT_ELU1) {
+                // elu(x) + 1 = x + 1 (x > 0) or exp(x), the pair's x + 1 in one op
+                const float2 p1 = f2_split(f2_add(x, f2_splat(1.f)));
+                y = f2_make(__float_as_uint(a > 0.f ? p1.x : __expf(a)),
+                            __float_as_uint(b > 0.f ? p1.y : __expf(b)));
+              } else {
+                y = f2_make(__float_as_uint(activate<ACT, true>(a)), __float_as_uint(activate<ACT, true>(b)));
+              }
+              packed[i] = pack_bf16x2(scaled ? f2_mul(y, tscale2) : y);
             }
           }
           // single staging buffer per warp: the previous store must have read it
@@ -430,11 +443,11 @@ enum PhiTiling { kTile256 = 0, kTile128 = 1, kTilePair = 2 };
 // Pairs of CTAs that can be resident at once (a pair needs two SMs of one
 // GPC), per device; 0 if the query failed.
 static int pair_slots() {
-  static int cached[64];
-  static bool done[64];
+  static std::atomic<int> cached[64];  // 0: not queried yet; else count + 1
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (!done[dev]) {
+  int known = cached[dev].load(std::memory_order_relaxed);
+  if (known == 0) {
     int n = 0;
     const auto kern = phi_gemm_sm100_kernel<FAKLA_ACT_ELU1, BN, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -453,10 +466,10 @@ static int pair_slots() {
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
     (void)cudaGetLastError();
-    cached[dev] = n;
-    done[dev] = true;
+    known = n + 1;  // the same value from any thread that gets here first
+    cached[dev].store(known, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return known - 1;
 }
 
 // CTA pairs when N allows 256-wide tiles and there are enough 256 x 256
