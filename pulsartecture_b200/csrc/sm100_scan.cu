@@ -102,7 +102,8 @@ enum Bar {
   kDrain,
   kKFree,   // unnormalised modes: the single K tile read by MMA4
   kRow0,    // (4) per output warp: its 32 rows of the epilogue's row tensor landed
-  kNumBars = kRow0 + 4
+  kFullV0 = kRow0 + 4,  // (kStages) forward: the V tile of a stage landed (Q, K: kFull0)
+  kNumBars = kFullV0 + kStages
 };
 static_assert(kNumBars * 8 + 8 <= kHeadBytes, "barrier area");
 
@@ -462,6 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   // which its output warps (not MMA3's commit) hand back to the producer.
   constexpr bool kRowTile = kGrad || MODE == kScanRevCol;
   constexpr bool kStageInV = MODE == kScanRevCol;
+  // The forward loads Q and K (needed first, by MMA1 and MMA2) apart from V
+  // (needed from MMA4 on) and stages its output in the V tile: the Q and K
+  // tiles of a stage are refilled as soon as MMA4 has read them, and only V
+  // waits for the output stores of the chunk two back, so those stores stay
+  // off the path to the next MMA1.
+  constexpr bool kSplitV = MODE == kScanNormal;
   // Vectors shared by every row of a chunk, broadcast from shared memory in
   // the unused rows of the two 1 KB N=16 operand atoms (with kZ, rows 0-1 of
   // both hold ZK and rows 4-5 of M0 ONES; the other rows only feed result
@@ -474,6 +481,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   float* mhi_sm = reinterpret_cast<float*>(sM0 + 1024 + 768);
   float* bcol_sm = reinterpret_cast<float*>(sM0);
   auto k_tile = [&](int st) { return sK + (kRaw ? 0 : st * kTile); };
+  // The forward's output epilogue is split by columns: the output warps take
+  // columns 0-63 of each chunk and the state warps, idle between their state
+  // refreshes, columns 64-127 (128-wide heads), which shortens the chain
+  // output -> OFree -> next chunk's MMA2 that sets the chunk period.
+  const bool split_o = MODE == kScanNormal && args.hd == 128;
   // first token of this CTA's chunk i
   auto chunk_t0 = [&](int i) {
     const int ci = c0 + i;
@@ -483,15 +495,16 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kFull0 + s], 1);
-      mbar_init(&bars[kEmpty0 + s], kStageInV ? 4 : 1);
-      mbar_init(&bars[kEmptyQ0 + s], 4);
+      mbar_init(&bars[kEmpty0 + s], kSplitV ? (split_o ? 8 : 4) : (kStageInV ? 4 : 1));
+      mbar_init(&bars[kEmptyQ0 + s], kSplitV ? 1 : 4);
+      mbar_init(&bars[kFullV0 + s], 1);
     }
     mbar_init(&bars[kBarP], 1);
     mbar_init(&bars[kBarS], 1);
     mbar_init(&bars[kBarO], 1);
     mbar_init(&bars[kE1Done], 4);
     mbar_init(&bars[kSReady], 4);
-    mbar_init(&bars[kOFree], 4);
+    mbar_init(&bars[kOFree], split_o ? 8 : 4);
     mbar_init(&bars[kKReady], 4);
     mbar_init(&bars[kDrain], 1);
     mbar_init(&bars[kKFree], 1);
@@ -534,10 +547,38 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      int issued = 0;
+      int issued = 0, issued_v = 0;
       for (int i = 0; i < nch && !*abort_flag; ++i) {
         const int st = i & 1;
         const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+        if constexpr (kSplitV) {
+          const int t0 = chunk_t0(i);
+          // Q, K of chunk i: MMA1-MMA4 of chunk i-2 have read the stage
+          if (!mbar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
+            report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          uint64_t* fb = &bars[kFull0 + st];
+          mbar_arrive_expect_tx(fb, 2 * na * kAtom);
+          for (int a = 0; a < na; ++a) {
+            tma_load_4d(sQ + st * kTile + a * kAtom, &tmQ, fb, a * 64, h, t0, b);
+            tma_load_4d(sK + st * kTile + a * kAtom, &tmK, fb, a * 64, h, t0, b);
+          }
+          ++issued;
+          // V of chunk i: the stores of chunk i-2's output (staged in this
+          // V tile) have read it
+          if (!mbar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
+            report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          uint64_t* fv = &bars[kFullV0 + st];
+          mbar_arrive_expect_tx(fv, na * kAtom);
+          for (int a = 0; a < na; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fv, a * 64, h, t0, b);
+          ++issued_v;
+          continue;
+        }
         if (!mbar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
@@ -577,6 +618,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         // Let this CTA's own copies in flight land before the CTA exits.
         for (int i = issued - kStages; i < issued; ++i)
           if (i >= 0) (void)mbar_wait(&bars[kFull0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
+        for (int i = issued_v - kStages; i < issued_v; ++i)
+          if (i >= 0) (void)mbar_wait(&bars[kFullV0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
       }
     }
   } else if (warp == 1) {
@@ -625,6 +668,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
 #pragma unroll
           for (int j = 0; j < 8; ++j) mma_ss(tmem + kColDz, kdesc(aQ, j), zkdesc(aM0, j), idQZ, j > 0);
         }
+        if constexpr (kSplitV) {
+          ok = mbar_wait(&bars[kFullV0 + st], ph, kWaitNs);
+          if (!ok) break;
+          tc_fence_after();
+        }
         // MMA4 / MMA4b: S += K^T V, z += K^T 1 (A = K as M=f x K=s, MN-major)
 #pragma unroll
         for (int j = 0; j < 8; ++j) mma_ss(tmem + kColS, mndesc(aK, j), mndesc(aV, j), idKV, 1u);
@@ -635,6 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         // the last reader of the single K tile of the unnormalised modes
         if constexpr (kRaw) mma_commit(&bars[kKFree]);
         mma_commit(&bars[kBarS]);
+        if constexpr (kSplitV) mma_commit(&bars[kEmptyQ0 + st]);  // Q, K of this stage read
         ok = mbar_wait(&bars[kE1Done], par, kWaitNs);
         if (!ok) break;
         tc_fence_after();
@@ -659,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           }
         }
         mma_commit(&bars[kBarO]);
-        if constexpr (!kStageInV) mma_commit(&bars[kEmpty0 + st]);
+        if constexpr (!kStageInV && !kSplitV) mma_commit(&bars[kEmpty0 + st]);
       }
       if (!ok) {
         report_status(args.status, FAKLA_ERR_TIMEOUT);
@@ -862,7 +911,42 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSReady]);
       if (has_temp && i + 1 < nch) ok = scale_k(i + 1);
+      if (split_o && ok) {
+        // columns 64-127 of chunk i's output rows 32 q4 + lane (TMEM lane r)
+        const uint32_t par = (uint32_t)i & 1u;
+        ok = warp_wait(&bars[kBarO], par);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t dz0, dz1, rsr;
+        tmem_ld2(lane_addr + kColDz, dz0, dz1);
+        tmem_ld1(lane_addr + kColRs + par, rsr);
+        uint32_t va[32], vb[32];
+        tmem_ld32(lane_addr + kColO + 64u, va);
+        tmem_ld32(lane_addr + kColO + 96u, vb);
+        tmem_ld_wait();
+        const float inv =
+            1.f / (__uint_as_float(rsr) + (__uint_as_float(dz0) + __uint_as_float(dz1)) + kEps);
+        uint8_t* stg = sV + (i & 1) * kTile;  // the chunk's V tile, read by MMA4 and MMA3 before barO
+        stage_scaled_32(va, inv, stg, r, 64);
+        stage_scaled_32(vb, inv, stg, r, 96);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kOFree]);  // O may be overwritten now
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int t0 = chunk_t0(i) + 32 * q4;
+          if (t0 < args.T) {
+            tma_store_4d(&tmO, stg + kAtom + q4 * (32 * 128), 64, h, t0, b);
+            bulk_commit_group();
+            bulk_wait_group_read<0>();
+          }
+          mbar_arrive(&bars[kEmpty0 + (i & 1)]);  // the V tile may be refilled
+        }
+        __syncwarp();
+      }
     }
+    if (split_o && lane == 0) bulk_wait_group<0>();  // output stores complete before the CTA exits
     if (!ok) {
       report_status(args.status, FAKLA_ERR_TIMEOUT);
       *abort_flag = 1;
@@ -951,9 +1035,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           args.den_out[((int64_t)b * args.T + t_tok) * args.H + h] = den;
       }
       // Stage the normalised rows in this chunk's Q tile (its last readers,
-      // MMA1/MMA2/MMA2b, completed before barO), or in its V tile (MMA3, the
-      // last reader, completed with barO) ...
-      uint8_t* stg = (kStageInV ? sV : sQ) + st * kTile;
+      // MMA1/MMA2/MMA2b, completed before barO), or in its V tile (MMA4 and
+      // MMA3, the last readers, completed with barO) ...
+      uint8_t* stg = (kStageInV || kSplitV ? sV : sQ) + st * kTile;
       const uint8_t* rtile = sQ + st * kTile;
       if constexpr (kGrad) {
         // backward's forward pass: dden = -(bf16(g / den) . out), out in fp32;
@@ -975,7 +1059,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (live) args.dden_out[row] = -acc;
       } else if (!kAffine) {
 #pragma unroll 1
-        for (int cc = 0; cc < args.hd; cc += 64) {
+        for (int cc = 0; cc < (split_o ? 64 : args.hd); cc += 64) {
           uint32_t va[32], vb[32];
           tmem_ld32(lane_addr + kColO + (uint32_t)cc, va);
           tmem_ld32(lane_addr + kColO + (uint32_t)(cc + 32), vb);
@@ -1025,13 +1109,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       if (lane == 0) {
         const int t0 = chunk_t0(i) + 32 * q4;
         if (t0 < args.T && (!kGrad || args.dnum_store)) {
-          for (int a = 0; a < na; ++a)
+          for (int a = 0; a < (split_o ? 1 : na); ++a)
             tma_store_4d(&tmO, stg + a * kAtom + q4 * (32 * 128), a * 64, h, t0, b);
           bulk_commit_group();
           bulk_wait_group_read<0>();
         }
-        mbar_arrive(&bars[kEmptyQ0 + st]);  // the Q tile may be refilled
-        if (kStageInV) mbar_arrive(&bars[kEmpty0 + st]);  // ... and the V tile
+        if (!kSplitV) mbar_arrive(&bars[kEmptyQ0 + st]);  // the Q tile may be refilled
+        if (kStageInV || kSplitV) mbar_arrive(&bars[kEmpty0 + st]);  // ... the V tile
       }
       __syncwarp();
       ++done;
