@@ -534,6 +534,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       reinterpret_cast<uint4*>(base)[o % kPer] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  // kScanRowAdd's centring vector, read by the output warps: m[0:64] in rows
+  // 6-7 of M0, m[64:128] in rows 6-7 of M1 (zero without centring, so that
+  // sigma * m is 0 whatever those rows held before)
+  if (MODE == kScanRowAdd && threadIdx.x < 128) {
+    const int f = threadIdx.x;
+    const float mf = (args.mvec != nullptr && f < args.hd) ? args.mvec[(int64_t)bh_idx * args.hd + f] : 0.f;
+    (f < 64 ? mlo_sm[f] : mhi_sm[f - 64]) = mf;
+  }
   fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -960,11 +968,6 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
     // centring vector) through shared memory and stop together (a named
     // barrier that ORs their wait results; every wait before it is bounded).
     const bool centre = MODE == kScanRowAdd && args.mvec != nullptr;
-    if (kAffine) {
-      if (centre)
-        (r < 64 ? mlo_sm[r] : mhi_sm[r - 64]) = r < args.hd ? args.mvec[(int64_t)bh_idx * args.hd + r] : 0.f;
-      named_barrier_sync(1, 128);
-    }
     // running chunk vector of the affine modes (feature r)
     float run = (kAffine && r < args.hd && args.vec_init != nullptr)
                     ? args.vec_init[(int64_t)bh_idx * args.hd + r] : 0.f;
