@@ -23,9 +23,15 @@
 //   warps 2-5   (P)  inclusive mask + hi/lo split of P, row sums; k*temp
 //   warps 6-9   (S)  state refresh: S (TMEM fp32) -> bf16 smem operand,
 //                    z -> hi/lo operand; initial state in, final state out
-//   warps 10-13 (O)  normalise O into the chunk's Q tile (dead by then) and
-//                    TMA-store it; the Q half of a stage is released after
-//                    that store has read it, the K/V half after MMA3
+//   warps 10-13 (O)  normalise O into a dead tile of the chunk and TMA-store
+//                    it. The forward stages in the V tile (its readers MMA4
+//                    and MMA3 are done at barO): Q and K of a stage come on
+//                    one barrier and are refilled once MMA4 has read them, V
+//                    on its own and refilled once the stores have read it;
+//                    with heads of 128 the S warps, idle between refreshes,
+//                    normalise and store columns 64-127. The backward modes
+//                    stage in the Q tile (or, mode 3, the V tile) and refill
+//                    Q after the stores, K/V after MMA3.
 // so the mask of chunk c+1 overlaps the normalisation of chunk c and the
 // state refresh, and the tensor pipe sees MMA2/MMA4 of one chunk between
 // MMA1 and MMA3 of the next.
