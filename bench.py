@@ -436,6 +436,56 @@ def run_longctx(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- feature-map mixer
+def run_mixer(args):
+    """KernelFeatureMixer forward (inference, bf16) on the prefill's q rows:
+    x (8*4096, 2048) -> three base maps of 2048 features each
+    (LearnablePositiveMap elu+1, RandomFourierFeatures and
+    OrthogonalRandomFeatures, 1024 projections each with cos/sin), a GateNet
+    over the same x and the softmax-weighted sum. Prints the time per forward,
+    tokens/s, the base-map GEMM rate against the measured tensor peak and the
+    mix kernel's HBM rate."""
+    from pulsartecture_b200.kernels import (KernelFeatureMixer, LearnablePositiveMap, OrthogonalRandomFeatures,
+                                            RandomFourierFeatures)
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    maps = [LearnablePositiveMap(IN_DIM, H * D), RandomFourierFeatures(IN_DIM, H * D, gamma=0.02),
+            OrthogonalRandomFeatures(IN_DIM, H * D, gamma=0.02)]
+    m = KernelFeatureMixer(maps, gate_input_dim=IN_DIM).to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(5)
+    rows = B * T
+    x = (torch.randn(rows, IN_DIM, generator=g, device=dev) / math.sqrt(D)).bfloat16()
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            m(x)
+        torch.cuda.synchronize()
+        ms = time_loop(lambda: m(x), args.steps, stream) / args.steps
+        map_ms = []
+        for fm in m.feature_maps:
+            fm(x)
+            map_ms.append(time_loop(lambda: fm(x), args.steps, stream) / args.steps)
+        y = m(x)
+    torch.cuda.synchronize()
+    _, tflops_burst, _, _ = peaks()
+    F = H * D
+    # base maps: the LearnablePositiveMap GEMM (F outputs) and F/2 projections
+    # for each of the two Fourier maps; the gate GEMM (3 outputs) is negligible
+    gemm_flops = 2.0 * rows * IN_DIM * (F + F // 2 + F // 2)
+    mix_bytes = (len(maps) + 1) * rows * F * 2  # read every map's features once, write the mix
+    line = {"only": "mixer", "workload": "KernelFeatureMixer([LPM elu+1, RFF, ORF], GateNet) forward, x (32768, 2048) "
+                                         "bf16 -> 2048 features",
+            "ms": round(ms, 4), "tokens_per_s": round(rows / ms * 1e3, 1),
+            "base_map_ms": {"lpm": round(map_ms[0], 4), "rff": round(map_ms[1], 4), "orf": round(map_ms[2], 4)},
+            "base_map_gemm_flops": gemm_flops, "gemm_tflops_if_alone": round(gemm_flops / ms / 1e9, 1),
+            "frac_of_tensor_peak_whole_forward": round(gemm_flops / ms / 1e9 / tflops_burst, 4),
+            "mix_bytes": mix_bytes, "finite": bool(torch.isfinite(y).all().item())}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- LM harness
 def run_lm(args):
     """Forward of the package's own end-to-end LM composition (lm_harness.py:
@@ -530,7 +580,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-module", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx"],
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx", "mixer"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -542,6 +592,8 @@ def main():
         return run_lm(args)
     if args.only == "longctx":
         return run_longctx(args)
+    if args.only == "mixer":
+        return run_mixer(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"

@@ -67,6 +67,19 @@ template <int BNT, bool PAIR>
 constexpr size_t kSmemBytesT = 1024 /*align slack*/ +
                                (size_t)kStagesT<BNT, PAIR> * kStageBytesT<BNT, PAIR> + kOutBytes + 256;
 
+// x - 2 pi k with k = round(x / (2 pi)): the cos/sin argument brought into
+// [-pi, pi] (Cody-Waite reduction with 2 pi split into a float head and the
+// remainder, both subtracted by fma), where the hardware sin/cos are accurate
+// to about 2^-21 absolute, far below the bf16 rounding of the output (the
+// output is rounded to bf16; fp32 maps use sincosf on the CUDA cores).
+__device__ __forceinline__ float reduce_2pi(float x) {
+  constexpr float kInv2Pi = 0.159154943091895336f;
+  constexpr float k2PiHi = 6.28318548202514648f;    // float(2 pi)
+  constexpr float k2PiLo = -1.7484556025237907e-07f;  // 2 pi - float(2 pi)
+  const float k = rintf(x * kInv2Pi);
+  return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+}
+
 struct PhiArgs {
   const __nv_bfloat16* bias;   // [N] or null
   float scale;                 // FAKLA_ACT_COSSIN output scale
@@ -354,8 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             const float2 ab = f2_split(x);
             const float a = ab.x, b = ab.y;
             if constexpr (ACT == FAKLA_ACT_COSSIN) {
-              const float fa = pass == 0 ? cosf(a) : sinf(a);
-              const float fb = pass == 0 ? cosf(b) : sinf(b);
+              const float ra = reduce_2pi(a), rb = reduce_2pi(b);
+              const float fa = pass == 0 ? __cosf(ra) : __sinf(ra);
+              const float fb = pass == 0 ? __cosf(rb) : __sinf(rb);
               packed[i] = pack_bf16x2(fa * args.scale * tscale, fb * args.scale * tscale);
             } else if (ident) {
               packed[i] = pack_bf16x2(x);
