@@ -86,6 +86,91 @@ __global__ void __launch_bounds__(256) phi_simt_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// The same map for narrow outputs (N <= kSkinnyN, e.g. a mixer's gate logits
+// over a few base maps): one warp per row, which streams the row once with
+// 16-byte loads (8 elements per lane and step) and keeps the N dot products in
+// registers; W (N x K) stays in L1. A 64x64 tile would leave all but N of its
+// 64 columns idle and read x with short accesses.
+// ---------------------------------------------------------------------------
+constexpr int kSkinnyN = 16;
+
+template <typename T>
+__device__ __forceinline__ void load8_f32(const T* p, float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+}
+
+template <typename T, int ACT, int NM>
+__global__ void __launch_bounds__(256) phi_skinny_kernel(
+    const T* __restrict__ x, const T* __restrict__ W, const T* __restrict__ bias,
+    const T* __restrict__ temp, T* __restrict__ out, int64_t rows, int64_t K,
+    int64_t N, int64_t heads, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * K;
+  float acc[NM];
+#pragma unroll
+  for (int n = 0; n < NM; ++n) acc[n] = 0.f;
+  // K % 8 == 0 and 16-byte aligned rows (checked by the launcher); two
+  // 8-element pieces of the row per step, both loaded before either is used
+  for (int64_t k = (int64_t)lane * 8; k < K; k += 512) {
+    const bool two = k + 256 < K;
+    float xv[2][8];
+    load8_f32(xr + k, xv[0]);
+    if (two) load8_f32(xr + k + 256, xv[1]);
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      if (h2 == 1 && !two) break;
+#pragma unroll
+      for (int n = 0; n < NM; ++n) {
+        if (n < N) {
+          float wv[8];
+          load8_f32(W + n * K + k + h2 * 256, wv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[n] = fmaf(xv[h2][e], wv[e], acc[n]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NM; ++n) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
+  }
+  // lane n writes output column n
+  float pre = 0.f;
+#pragma unroll
+  for (int n = 0; n < NM; ++n)
+    if (lane == n) pre = acc[n];
+  if (lane < N) {
+    const int64_t m = N / heads;
+    pre += bias ? to_f32(bias[lane]) : 0.f;
+    const float tv = temp ? to_f32(temp[row * heads + lane / m]) : 1.f;
+    if constexpr (ACT == FAKLA_ACT_COSSIN) {
+      float sn, cs;
+      sincosf(pre, &sn, &cs);
+      out[row * 2 * N + lane] = from_f32<T>(cs * scale * tv);
+      out[row * 2 * N + N + lane] = from_f32<T>(sn * scale * tv);
+    } else {
+      out[row * N + lane] = from_f32<T>(activate<ACT, false>(pre) * tv);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Causal FA-KLA scan, one CTA per (b,h) sequence, token-sequential.
 // Thread (g, dv) keeps S[f][dv] for f = g, g+G, g+2G, ... in registers
 // (G = 256 / Dv feature groups) and its slice of z; per token it updates its
@@ -315,6 +400,18 @@ static cudaError_t launch_phi_simt_t(const void* x, const void* W, const void* b
                                      const void* temp, void* out, int64_t rows,
                                      int64_t K, int64_t N, int64_t heads, float scale,
                                      cudaStream_t stream) {
+  const bool aligned16 = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W)) & 15u) == 0;
+  if (N <= kSkinnyN && K % 8 == 0 && aligned16) {
+    const int64_t blocks = (rows + 7) / 8;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+    if (N <= 4)
+      phi_skinny_kernel<T, ACT, 4><<<(unsigned)blocks, 256, 0, stream>>>(
+          (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads, scale);
+    else
+      phi_skinny_kernel<T, ACT, kSkinnyN><<<(unsigned)blocks, 256, 0, stream>>>(
+          (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads, scale);
+    return cudaGetLastError();
+  }
   dim3 grid((unsigned)((N + kPhiTile - 1) / kPhiTile), (unsigned)((rows + kPhiTile - 1) / kPhiTile));
   phi_simt_kernel<T, ACT><<<grid, 256, 0, stream>>>(
       (const T*)x, (const T*)W, (const T*)bias, (const T*)temp, (T*)out, rows, K, N, heads, scale);
