@@ -491,13 +491,88 @@ __global__ void __launch_bounds__(256) mix_features_kernel(const T* __restrict__
   for (int v = 0; v < VEC; ++v) dst[v] = from_f32<T>(acc[v]);
 }
 
+// The same combination for bf16 and up to kMixFast maps with 8 features per
+// thread (16-byte loads and stores): the gate weights and every map's 8
+// features are held in registers, all the map loads issued before any is
+// used. The arithmetic and its order are those of mix_features_kernel.
+constexpr int kMixFast = 8;
+
+template <typename T>
+__device__ __forceinline__ void store8_from_f32(T* p, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) mix_features_fast_kernel(const T* __restrict__ feats,
+                                                                const T* __restrict__ logits,
+                                                                T* __restrict__ out, int64_t rows,
+                                                                int n_maps, int64_t F) {
+  const int64_t per_row = F / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const int64_t r = idx / per_row;
+  const int64_t f0 = (idx % per_row) * 8;
+  // the maps' 8 features as raw bf16 (16 bytes each), converted when used
+  uint4 x[kMixFast];
+#pragma unroll
+  for (int i = 0; i < kMixFast; ++i)
+    if (i < n_maps) x[i] = __ldg(reinterpret_cast<const uint4*>(feats + ((int64_t)i * rows + r) * F + f0));
+  float w[kMixFast];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMixFast; ++i) {
+    w[i] = i < n_maps ? to_f32(logits[r * n_maps + i]) : -INFINITY;
+    mx = fmaxf(mx, w[i]);
+  }
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMixFast; ++i) {
+    if (i < n_maps) {
+      w[i] = expf(w[i] - mx);
+      den += w[i];
+    }
+  }
+  const float inv = 1.f / den;
+  float acc[8];
+#pragma unroll
+  for (int v = 0; v < 8; ++v) acc[v] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMixFast; ++i) {
+    if (i < n_maps) {
+      const float wi = to_f32(from_f32<T>(w[i] * inv));
+      const uint32_t u[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        acc[2 * v] = fmaf(wi, __uint_as_float(u[v] << 16), acc[2 * v]);
+        acc[2 * v + 1] = fmaf(wi, __uint_as_float(u[v] & 0xffff0000u), acc[2 * v + 1]);
+      }
+    }
+  }
+  store8_from_f32(out + r * F + f0, acc);
+}
+
 template <typename T>
 static cudaError_t launch_mix_t(const void* feats, const void* logits, void* out, int64_t rows,
                                 int64_t n_maps, int64_t F, cudaStream_t stream) {
   const bool vec = F % 8 == 0 && ((uintptr_t)feats & 15u) == 0 && ((uintptr_t)out & 15u) == 0;
   const int64_t threads = rows * (vec ? F / 8 : F);
   const unsigned grid = (unsigned)((threads + 255) / 256);
-  if (vec)
+  if (vec && n_maps <= kMixFast && sizeof(T) == 2)
+    mix_features_fast_kernel<T><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
+                                                        rows, (int)n_maps, F);
+  else if (vec)
     mix_features_kernel<T, 8><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
                                                        rows, (int)n_maps, F);
   else
