@@ -129,6 +129,30 @@ def lpm_init(in_dim, feat, seed=0):
     return m.weight.detach().clone(), m.bias.detach().clone()
 
 
+def bind_near_gpu(device_index: int):
+    """Restrict this process's threads to the CPUs NVML lists as closest to
+    the GPU (its NUMA node), so that host buffers first touched afterwards
+    live in that node's memory; returns the previous CPU set to restore, or
+    None when NVML gives nothing usable. With one process per GPU, every
+    rank's pinned copies then come from the memory next to its own GPU."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+        words = ((os.cpu_count() or 64) + 63) // 64
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {64 * w + b for w, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+        prev = os.sched_getaffinity(0)
+        cpus &= prev
+        if not cpus or cpus == prev:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return prev
+    except Exception:
+        return None
+
+
 def sync_barrier(world):
     if world > 1:
         dist.barrier()
@@ -680,6 +704,7 @@ def main():
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        prev_cpus = bind_near_gpu(dev.index if dev.index is not None else 0)
         hq = q.cpu().pin_memory()
         hk = k.cpu().pin_memory()
         hv = v.cpu().pin_memory()
@@ -733,6 +758,9 @@ def main():
         del hq, hk, hv, hout
         from pulsartecture_b200.backend.interface import release_host_pipelines
         release_host_pipelines()
+        if prev_cpus is not None:
+            os.sched_setaffinity(0, prev_cpus)
+        e2e["host_cpus"] = "GPU-local NUMA node (NVML CPU affinity)" if prev_cpus is not None else "unchanged"
 
     # ---- decode: batch 256, H=32, D=M=128, fp32 state, 1024 steps
     decode = None
