@@ -514,53 +514,61 @@ __device__ __forceinline__ void store8_from_f32(T* p, const float (&f)[8]) {
   }
 }
 
-template <typename T>
+template <typename T, int NMAX, int CH>
 __global__ void __launch_bounds__(256) mix_features_fast_kernel(const T* __restrict__ feats,
                                                                 const T* __restrict__ logits,
                                                                 T* __restrict__ out, int64_t rows,
                                                                 int n_maps, int64_t F) {
-  const int64_t per_row = F / 8;
+  // CH consecutive 8-feature pieces per thread (F % (8 CH) == 0)
+  const int64_t per_row = F / (8 * CH);
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * per_row) return;
   const int64_t r = idx / per_row;
-  const int64_t f0 = (idx % per_row) * 8;
-  // the maps' 8 features as raw bf16 (16 bytes each), converted when used
-  uint4 x[kMixFast];
+  const int64_t f0 = (idx % per_row) * 8 * CH;
+  // the maps' features as raw bf16 (16 bytes per piece), converted when used
+  uint4 x[NMAX][CH];
 #pragma unroll
-  for (int i = 0; i < kMixFast; ++i)
-    if (i < n_maps) x[i] = __ldg(reinterpret_cast<const uint4*>(feats + ((int64_t)i * rows + r) * F + f0));
-  float w[kMixFast];
+  for (int i = 0; i < NMAX; ++i)
+    if (i < n_maps) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        x[i][c] = __ldg(reinterpret_cast<const uint4*>(feats + ((int64_t)i * rows + r) * F + f0) + c);
+    }
+  float w[NMAX];
   float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMixFast; ++i) {
+  for (int i = 0; i < NMAX; ++i) {
     w[i] = i < n_maps ? to_f32(logits[r * n_maps + i]) : -INFINITY;
     mx = fmaxf(mx, w[i]);
   }
   float den = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMixFast; ++i) {
+  for (int i = 0; i < NMAX; ++i) {
     if (i < n_maps) {
       w[i] = expf(w[i] - mx);
       den += w[i];
     }
   }
   const float inv = 1.f / den;
-  float acc[8];
 #pragma unroll
-  for (int v = 0; v < 8; ++v) acc[v] = 0.f;
+  for (int c = 0; c < CH; ++c) {
+    float acc[8];
 #pragma unroll
-  for (int i = 0; i < kMixFast; ++i) {
-    if (i < n_maps) {
-      const float wi = to_f32(from_f32<T>(w[i] * inv));
-      const uint32_t u[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+    for (int v = 0; v < 8; ++v) acc[v] = 0.f;
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        acc[2 * v] = fmaf(wi, __uint_as_float(u[v] << 16), acc[2 * v]);
-        acc[2 * v + 1] = fmaf(wi, __uint_as_float(u[v] & 0xffff0000u), acc[2 * v + 1]);
+    for (int i = 0; i < NMAX; ++i) {
+      if (i < n_maps) {
+        const float wi = to_f32(from_f32<T>(w[i] * inv));
+        const uint32_t u[4] = {x[i][c].x, x[i][c].y, x[i][c].z, x[i][c].w};
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          acc[2 * v] = fmaf(wi, __uint_as_float(u[v] << 16), acc[2 * v]);
+          acc[2 * v + 1] = fmaf(wi, __uint_as_float(u[v] & 0xffff0000u), acc[2 * v + 1]);
+        }
       }
     }
+    store8_from_f32(out + r * F + f0 + 8 * c, acc);
   }
-  store8_from_f32(out + r * F + f0, acc);
 }
 
 template <typename T>
@@ -569,9 +577,12 @@ static cudaError_t launch_mix_t(const void* feats, const void* logits, void* out
   const bool vec = F % 8 == 0 && ((uintptr_t)feats & 15u) == 0 && ((uintptr_t)out & 15u) == 0;
   const int64_t threads = rows * (vec ? F / 8 : F);
   const unsigned grid = (unsigned)((threads + 255) / 256);
-  if (vec && n_maps <= kMixFast && sizeof(T) == 2)
-    mix_features_fast_kernel<T><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
-                                                        rows, (int)n_maps, F);
+  if (vec && n_maps <= 4 && sizeof(T) == 2 && F % 16 == 0)
+    mix_features_fast_kernel<T, 4, 2><<<(unsigned)((rows * (F / 16) + 255) / 256), 256, 0, stream>>>(
+        (const T*)feats, (const T*)logits, (T*)out, rows, (int)n_maps, F);
+  else if (vec && n_maps <= kMixFast && sizeof(T) == 2)
+    mix_features_fast_kernel<T, kMixFast, 1><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits,
+                                                                     (T*)out, rows, (int)n_maps, F);
   else if (vec)
     mix_features_kernel<T, 8><<<grid, 256, 0, stream>>>((const T*)feats, (const T*)logits, (T*)out,
                                                        rows, (int)n_maps, F);
