@@ -43,6 +43,9 @@ def _inputs(rows, K, N, seed, dtype, dev, xscale=1.0):
     (600, 192, 384, torch.bfloat16),     # tensor-core tiles, N an odd multiple of 128
     (20000, 128, 1024, torch.bfloat16),  # CTA-pair 256x256 tiles (316 of them)
     (19999, 192, 512, torch.bfloat16),   # CTA-pair tiles, last one ragged (rank 1 partly past the end)
+    (5000, 2048, 3, torch.bfloat16),     # narrow output (a gate): one warp per row
+    (333, 40, 16, torch.float32),        # narrow output, fp32, K smaller than a warp's 256-wide step
+    (64, 36, 5, torch.bfloat16),         # narrow output with K % 8 != 0: the tiled CUDA-core path
     (77, 96, 40, torch.bfloat16),        # CUDA-core shape
     (300, 200, 96, torch.float32),       # fp32
 ])
