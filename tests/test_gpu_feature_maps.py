@@ -84,7 +84,10 @@ def test_feature_map_cos_sin(cuda, rows, K, P, dtype):
 
 # ----------------------------------------------------------------- fakla_mix_features
 @pytest.mark.parametrize("n,rows,Fdim,dtype", [(3, 500, 128, torch.bfloat16), (2, 37, 33, torch.float32),
-                                               (5, 64, 256, torch.float32)])
+                                               (5, 64, 256, torch.float32),
+                                               (6, 300, 64, torch.bfloat16),   # bf16, 5-8 maps: 8 features a thread
+                                               (4, 100, 24, torch.bfloat16),   # bf16, F % 16 != 0
+                                               (12, 40, 32, torch.bfloat16)])  # bf16, more than 8 maps
 def test_mix_features(cuda, n, rows, Fdim, dtype):
     from pulsartecture_b200.backend.interface import mix_features
 
