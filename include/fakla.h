@@ -225,7 +225,8 @@ typedef enum {
  *          holds scale * cos(p_n) and column n_out + n holds scale * sin(p_n),
  *          p = x W^T + bias. `scale` is ignored by the other activations.
  * The tensor-core path serves BF16 with in_dim % 64 == 0, n_out % 128 == 0
- * and 16-byte aligned pointers; other shapes and F32 run on CUDA cores.
+ * and 16-byte aligned pointers; other shapes and F32 run on CUDA cores
+ * (n_out <= 16 with in_dim % 8 == 0, e.g. gate logits, one warp per row).
  */
 int fakla_feature_map(const void* x, const void* W, const void* bias, void* out,
                       int64_t rows, int64_t in_dim, int64_t n_out, int act,
