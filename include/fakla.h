@@ -343,8 +343,11 @@ size_t fakla_decode_workspace_bytes(int64_t N, int64_t in_dim, int64_t H,
  * process exit; nothing is allocated per call.
  * Limit: 2 * N * H * M * sizeof(element) <= FAKLA_NOALLOC_SCRATCH_BYTES
  * (e.g. N=256, H=32, M=128 in bf16 uses 4 MiB); larger steps are rejected with
- * FAKLA_ERR_UNSUPPORTED. The first call on a device looks up the array's
- * device address; make it before any stream capture. All calls share the one
+ * FAKLA_ERR_UNSUPPORTED (argument errors are reported first, as fakla_decode
+ * reports them). The first call on a device looks up the array's device
+ * address; make it before any stream capture. The address is kept for that
+ * device's current CUDA context and looked up again once that context has
+ * been destroyed and recreated (cudaDeviceReset). All calls share the one
  * array: calls whose GPU work overlaps race on it and must be serialised by
  * the caller. Nothing in it needs to start at zero (each call writes all the
  * scratch it reads).

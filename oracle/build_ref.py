@@ -32,7 +32,10 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_DEFAULT = "/root/reference"
+# Root of the reference checkout (the directory holding ultra_rwka/): the
+# `ref_root` argument, else this environment variable; with neither, build()
+# only reports the prebuilt module.
+REF_ENV = "FAKLA_REFERENCE_ROOT"
 REF_SRC = "ultra_rwka/backend/cpp/cpu/cpu_kernels.cpp"
 REF_HDR = "ultra_rwka/backend/ include/common.h"
 OUT_DIR = os.path.join(HERE, "_ref")
@@ -44,10 +47,17 @@ def built_module_path() -> str | None:
     return hits[0] if hits else None
 
 
-def build(ref_root: str = REF_DEFAULT, verbose: bool = False) -> str | None:
-    """Compile the reference kernel; returns the .so path or None if the
-    reference checkout is absent (e.g. on a GPU host, which uses the prebuilt
-    file)."""
+def reference_root(ref_root: str | None = None) -> str | None:
+    return ref_root or os.environ.get(REF_ENV) or None
+
+
+def build(ref_root: str | None = None, verbose: bool = False) -> str | None:
+    """Compile the reference kernel; returns the .so path, or the prebuilt
+    one (None if never built) when no reference checkout is given or present
+    (e.g. on a GPU host, which uses the prebuilt file)."""
+    ref_root = reference_root(ref_root)
+    if ref_root is None:
+        return built_module_path()
     src = os.path.join(ref_root, REF_SRC)
     hdr = os.path.join(ref_root, REF_HDR)
     if not (os.path.isfile(src) and os.path.isfile(hdr)):
@@ -104,5 +114,7 @@ def load():
 
 
 if __name__ == "__main__":
-    p = build(sys.argv[1] if len(sys.argv) > 1 else REF_DEFAULT, verbose=True)
-    print(p)
+    root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if root is None:
+        sys.exit(f"usage: python oracle/build_ref.py REFERENCE_ROOT (or set {REF_ENV})")
+    print(build(root, verbose=True))

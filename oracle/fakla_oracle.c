@@ -60,15 +60,16 @@ void fakla_oracle_phi_f64(const double* x, const double* W, const double* bias,
  *   out_t = num * 1/(den + eps)  (159-162)
  * The output at t includes token t (inclusive causal).
  * S0/z0: initial state or NULL for zeros (the reference always starts at zero,
- * cpu_kernels.cpp:78-79). S1/z1: final state or NULL. temp NULL = all ones. */
-void fakla_oracle_attention_f64(const double* q, const double* k, const double* v,
-                                const double* temp, double* out, const double* S0,
-                                const double* z0, double* S1, double* z1, int64_t B,
-                                int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+ * cpu_kernels.cpp:78-79). S1/z1: final state or NULL. temp NULL = all ones.
+ * Returns 0, or -1 (nothing written) for head dims outside [1, 256]. */
+int fakla_oracle_attention_f64(const double* q, const double* k, const double* v,
+                               const double* temp, double* out, const double* S0,
+                               const double* z0, double* S1, double* z1, int64_t B,
+                               int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+  if (Df < 1 || Dv < 1 || Df > 256 || Dv > 256) return -1;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int64_t bh = 0; bh < B * H; ++bh) {
     const int64_t b = bh / H, h = bh % H;
-    if (Df > 256 || Dv > 256) continue; /* oracle limit; callers check */
     double* S = (double*)malloc(sizeof(double) * (size_t)(Df * Dv + 2 * Df + Dv));
     double* z = S + Df * Dv;
     double* kt = z + Df;
@@ -99,20 +100,22 @@ void fakla_oracle_attention_f64(const double* q, const double* k, const double* 
     if (z1) memcpy(z1 + bh * Df, z, sizeof(double) * Df);
     free(S);
   }
+  return 0;
 }
 
 /* Same recurrence in float arithmetic, statement for statement as the
  * reference's fp32 instantiation (scalar_t = float, cpu_kernels.cpp:82-162):
  * float k~ buffer, float S/z, float reciprocal of (den + 1e-12f). Only the
- * summation order of the BLAS calls (matmul/dot) may differ. */
-void fakla_oracle_attention_f32(const float* q, const float* k, const float* v,
-                                const float* temp, float* out, const float* S0,
-                                const float* z0, float* S1, float* z1, int64_t B,
-                                int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+ * summation order of the BLAS calls (matmul/dot) may differ.
+ * Returns 0, or -1 (nothing written) for head dims outside [1, 256]. */
+int fakla_oracle_attention_f32(const float* q, const float* k, const float* v,
+                               const float* temp, float* out, const float* S0,
+                               const float* z0, float* S1, float* z1, int64_t B,
+                               int64_t T, int64_t H, int64_t Df, int64_t Dv) {
+  if (Df < 1 || Dv < 1 || Df > 256 || Dv > 256) return -1;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int64_t bh = 0; bh < B * H; ++bh) {
     const int64_t b = bh / H, h = bh % H;
-    if (Df > 256 || Dv > 256) continue; /* oracle limit; callers check */
     float* S = (float*)malloc(sizeof(float) * (size_t)(Df * Dv + 2 * Df + Dv));
     float* z = S + Df * Dv;
     float* kt = z + Df;
@@ -143,6 +146,7 @@ void fakla_oracle_attention_f32(const float* q, const float* k, const float* v,
     if (z1) memcpy(z1 + bh * Df, z, sizeof(float) * Df);
     free(S);
   }
+  return 0;
 }
 
 /* Round-to-nearest-even float -> bfloat16 -> float, as the device's

@@ -59,6 +59,7 @@ def _load():
             for name, p in (("fakla_oracle_attention_f64", _f64p), ("fakla_oracle_attention_f32", _f32p)):
                 fn = getattr(lib, name)
                 fn.argtypes = [p] * 9 + [_i64] * 5
+                fn.restype = ctypes.c_int
             lib.fakla_oracle_round_bf16.argtypes = [_f32p, _i64]
             _lib = lib
     return _lib
@@ -122,10 +123,12 @@ def attention(q, k, v, temp=None, S0=None, z0=None, precision: str = "f64"):
     out = np.empty((B, T, H, Dv), dt)
     S1 = np.empty((B, H, Df, Dv), dt)
     z1 = np.empty((B, H, Df), dt)
-    getattr(_load(), fn)(
+    rc = getattr(_load(), fn)(
         _ptr(qd, p), _ptr(kd, p), _ptr(vd, p), _ptr(td, p), _ptr(out, p),
         _ptr(S0d, p), _ptr(z0d, p), _ptr(S1, p), _ptr(z1, p), B, T, H, Df, Dv,
     )
+    if rc != 0:
+        raise ValueError(f"oracle attention rejected head dims Df={Df} Dv={Dv}")
     return out, S1, z1
 
 

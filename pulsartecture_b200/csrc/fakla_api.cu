@@ -57,12 +57,42 @@ extern "C" int fakla_version(void) { return FAKLA_VERSION; }
 __device__ int g_device_status_word;
 
 namespace {
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+template <typename Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+}  // namespace
+
+unsigned long long fakla_context_id() {
+  static const CtxGetCurrentFn get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id + 1;  // 0 stays "no context"
+}
+
+namespace {
 constexpr int kMaxDevices = 64;
+// Cached per device for the context they were queried in: a context that is
+// destroyed (cudaDeviceReset) and recreated gets a new id, and the cache is
+// refreshed on the next call instead of handing out a stale status address.
 struct DeviceInfo {
-  std::atomic<int> ready{0};
-  int* status = nullptr;
+  std::atomic<unsigned long long> ctx{0};
+  std::atomic<int*> status{nullptr};
   int sms = 0;
   int major = 0;
+  int* st() const { return status.load(std::memory_order_relaxed); }
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -75,18 +105,26 @@ DeviceInfo* device_info(int* err) {
     return nullptr;
   }
   DeviceInfo* d = &g_dev[dev];
-  if (d->ready.load(std::memory_order_acquire)) return d;
+  const unsigned long long cur = fakla_context_id();
+  if (cur != 0 && d->ctx.load(std::memory_order_acquire) == cur) return d;
   std::lock_guard<std::mutex> lk(g_dev_mu);
-  if (!d->ready.load(std::memory_order_relaxed)) {
-    e = cudaDeviceGetAttribute(&d->major, cudaDevAttrComputeCapabilityMajor, dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&d->status, g_device_status_word);
-    if (e != cudaSuccess) {
-      *err = cuda_fail(e, "device query");
-      return nullptr;
-    }
-    d->ready.store(1, std::memory_order_release);
+  if (cur != 0 && d->ctx.load(std::memory_order_relaxed) == cur) return d;
+  // These runtime calls also make the device's primary context current when
+  // the calling thread has none yet.
+  int major = 0, sms = 0;
+  int* status = nullptr;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&status, g_device_status_word);
+  if (e != cudaSuccess) {
+    *err = cuda_fail(e, "device query");
+    return nullptr;
   }
+  d->major = major;
+  d->sms = sms;
+  d->status.store(status, std::memory_order_relaxed);
+  // 0 (context id unavailable) keeps the entry uncached: queried again next call
+  d->ctx.store(fakla_context_id(), std::memory_order_release);
   return d;
 }
 
@@ -106,7 +144,7 @@ int require_device(DeviceInfo** out) {
 int* fakla_status_word() {
   int err;
   DeviceInfo* d = device_info(&err);
-  return d ? d->status : nullptr;
+  return d ? d->st() : nullptr;
 }
 
 int fakla_sm_count() {
@@ -216,7 +254,7 @@ int run_attention(const void* q, const void* k, const void* v, const void* temp,
   if (use_sm100_scan(dtype, q, k, v, out, S, B, T, H, Df, Dv)) {
     bool enc = false;
     cudaError_t e = fakla::launch_scan_sm100(q, k, v, temp, out, S, z, B, T, H, flags, workspace,
-                                             workspace_bytes, d->sms, stream, d->status, &enc, 0, Df);
+                                             workspace_bytes, d->sms, stream, d->st(), &enc, 0, Df);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
     return FAKLA_OK;
@@ -239,7 +277,7 @@ int run_phi(const void* x0, const void* x1, const void* W, const void* bias, con
   if (use_sm100_phi(dtype, x0, x1, W, out0, out1, bias, rows, K, N, heads)) {
     bool enc = false;
     cudaError_t e = fakla::launch_phi_sm100(x0, x1, W, bias, temp0, temp1, out0, out1, rows, K,
-                                            N, heads, act, scale, stream, d->status, &enc);
+                                            N, heads, act, scale, stream, d->st(), &enc);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "phi_sm100 launch");
     return FAKLA_OK;
@@ -356,7 +394,7 @@ extern "C" int fakla_attention_backward(const void* q, const void* k, const void
     bool enc = false;
     cudaError_t e = fakla::launch_backward_sm100(q, k, v, temp, dout, S0, z0, dS_final, dz_final,
                                                  dq, dk, dv, dtemp, dS0, dz0, B, T, H, Df, workspace,
-                                                 d->sms, (cudaStream_t)stream, d->status, &enc);
+                                                 d->sms, (cudaStream_t)stream, d->st(), &enc);
     if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
     if (e != cudaSuccess) return cuda_fail(e, "attention backward (sm100) launch");
     return FAKLA_OK;
@@ -545,7 +583,7 @@ extern "C" int fakla_qkv_prefill(const void* x, const void* W, const void* bias,
   uint8_t* buf = (uint8_t*)workspace;
   bool enc = false;
   cudaError_t e = fakla::launch_qkv_sm100(x, W, bias, temp, buf, rows, embed, H * M, H * Dv, H, st,
-                                          d->status, &enc);
+                                          d->st(), &enc);
   if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
   if (e != cudaSuccess) return cuda_fail(e, "qkv GEMM launch");
   const int64_t row_elems = 2 * H * M + H * Dv;
@@ -553,7 +591,7 @@ extern "C" int fakla_qkv_prefill(const void* x, const void* W, const void* bias,
   const void* phk = buf + (size_t)H * M * 2;
   const void* vv = buf + (size_t)2 * H * M * 2;
   e = fakla::launch_scan_sm100(phq, phk, vv, nullptr, out, S, z, B, T, H, flags, buf + need,
-                               workspace_bytes - need, d->sms, st, d->status, &enc, row_elems, M);
+                               workspace_bytes - need, d->sms, st, d->st(), &enc, row_elems, M);
   if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
   if (e != cudaSuccess) return cuda_fail(e, "scan_sm100 launch");
   return FAKLA_OK;
@@ -586,10 +624,9 @@ extern "C" size_t fakla_decode_workspace_bytes(int64_t N, int64_t in_dim, int64_
   return 2 * round_up((size_t)N * (size_t)H * (size_t)M * esize(dtype), 256);
 }
 
-extern "C" int fakla_decode(const void* q, const void* k, const void* v, const void* temp,
-                            const void* W, const void* bias, void* out, float* S, float* z,
-                            int64_t N, int64_t in_dim, int64_t H, int64_t M, int64_t Dv, int dtype,
-                            void* workspace, size_t workspace_bytes, void* stream) {
+int fakla_decode_check(const void* q, const void* k, const void* v, const void* W, const void* out,
+                       const float* S, const float* z, int64_t N, int64_t in_dim, int64_t H,
+                       int64_t M, int64_t Dv, int dtype) {
   int rc = check_dtype(dtype);
   if (rc) return rc;
   if (!q || !k || !v || !W || !out || !S || !z)
@@ -598,6 +635,15 @@ extern "C" int fakla_decode(const void* q, const void* k, const void* v, const v
     return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
   if (M > kMaxHeadDim || Dv > kMaxHeadDim)
     return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "head dims above %lld", (long long)kMaxHeadDim);
+  return FAKLA_OK;
+}
+
+extern "C" int fakla_decode(const void* q, const void* k, const void* v, const void* temp,
+                            const void* W, const void* bias, void* out, float* S, float* z,
+                            int64_t N, int64_t in_dim, int64_t H, int64_t M, int64_t Dv, int dtype,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = fakla_decode_check(q, k, v, W, out, S, z, N, in_dim, H, M, Dv, dtype);
+  if (rc) return rc;
   const size_t need = fakla_decode_workspace_bytes(N, in_dim, H, M, Dv, dtype);
   if (workspace == nullptr || workspace_bytes < need)
     return fakla_set_error(FAKLA_ERR_WORKSPACE, "decode needs %zu workspace bytes, got %zu", need,

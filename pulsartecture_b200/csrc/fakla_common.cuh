@@ -80,3 +80,11 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
 int fakla_set_error(int status, const char* fmt, ...);
 int* fakla_status_word();  // device address of the current device's status word
 int fakla_sm_count();      // SM count of the current device (cached)
+// Unique id (+1) of the calling thread's current CUDA context; 0 when there is
+// none yet or the driver cannot say. Caches of device addresses key on it.
+unsigned long long fakla_context_id();
+// fakla_decode's argument checks (dtype, pointers, sizes, head dims), all
+// but the workspace; FAKLA_OK or the error code with its message set.
+int fakla_decode_check(const void* q, const void* k, const void* v, const void* W, const void* out,
+                       const float* S, const float* z, int64_t N, int64_t in_dim, int64_t H,
+                       int64_t M, int64_t Dv, int dtype);

@@ -17,8 +17,10 @@
 //    phi(k)); larger requests are rejected with FAKLA_ERR_UNSUPPORTED and
 //    nothing is launched.
 //  * The first call on a device looks up the array's device address (with
-//    that device current) and caches it; make that first call before any
-//    stream capture.
+//    that device current) and caches it for that device's current CUDA
+//    context; make that first call before any stream capture. A call made
+//    after the context was destroyed and recreated (cudaDeviceReset) looks
+//    the address up again.
 //  * Every call uses the same array. Each call overwrites all of the scratch
 //    it reads (the phi kernel writes every phi(q)/phi(k) element before the
 //    state kernel reads it), so nothing has to start at zero; but calls whose
@@ -27,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "fakla_common.cuh"
@@ -38,7 +41,12 @@ static_assert(kScratchBytes % 256 == 0, "scratch size");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices];
+// Device address of the array per device, for the context it was looked up in.
+struct ScratchSlot {
+  std::atomic<unsigned long long> ctx{0};
+  std::atomic<void*> addr{nullptr};
+};
+ScratchSlot g_scratch[kMaxDevices];
 std::mutex g_scratch_mu;
 
 // Device address of g_noalloc_scratch on the current device (the host-side
@@ -50,16 +58,22 @@ int scratch_address(void** out) {
     return fakla_set_error(FAKLA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return fakla_set_error(FAKLA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return fakla_set_error(FAKLA_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s",
-                             cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
+  ScratchSlot& slot = g_scratch[dev];
+  const unsigned long long cur = fakla_context_id();
+  if (cur != 0 && slot.ctx.load(std::memory_order_acquire) == cur) {
+    *out = slot.addr.load(std::memory_order_relaxed);
+    return FAKLA_OK;
   }
-  *out = g_scratch_addr[dev];
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  void* p = nullptr;
+  // with the device current; creates its primary context if the thread has none
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return fakla_set_error(FAKLA_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s",
+                           cudaGetErrorString(e));
+  slot.addr.store(p, std::memory_order_relaxed);
+  slot.ctx.store(fakla_context_id(), std::memory_order_release);
+  *out = p;
   return FAKLA_OK;
 }
 }  // namespace
@@ -68,10 +82,10 @@ extern "C" int fakla_decode_noalloc(const void* q, const void* k, const void* v,
                                     const void* W, const void* bias, void* out, float* S, float* z,
                                     int64_t N, int64_t in_dim, int64_t H, int64_t M, int64_t Dv,
                                     int dtype, void* stream) {
-  if (dtype != FAKLA_F32 && dtype != FAKLA_BF16)
-    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "dtype %d is not FAKLA_F32 or FAKLA_BF16", dtype);
-  if (N < 1 || in_dim < 1 || H < 1 || M < 1 || Dv < 1)
-    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  // the argument checks of fakla_decode first, so a bad call reports its
+  // real error rather than a scratch-size one
+  int rc = fakla_decode_check(q, k, v, W, out, S, z, N, in_dim, H, M, Dv, dtype);
+  if (rc != FAKLA_OK) return rc;
   const size_t need = fakla_decode_workspace_bytes(N, in_dim, H, M, Dv, dtype);
   if (need > kScratchBytes)
     return fakla_set_error(FAKLA_ERR_UNSUPPORTED,
@@ -79,7 +93,7 @@ extern "C" int fakla_decode_noalloc(const void* q, const void* k, const void* v,
                            "holds %zu; use fakla_decode with a caller workspace",
                            need, kScratchBytes);
   void* scratch = nullptr;
-  int rc = scratch_address(&scratch);
+  rc = scratch_address(&scratch);
   if (rc != FAKLA_OK) return rc;
   return fakla_decode(q, k, v, temp, W, bias, out, S, z, N, in_dim, H, M, Dv, dtype, scratch,
                       kScratchBytes, stream);

@@ -2,7 +2,7 @@
 
 Run where the reference checkout is present (it is read, never copied):
 
-    python tests/golden/make_feature_golden.py [/root/reference]
+    python tests/golden/make_feature_golden.py REFERENCE_ROOT     (or set FAKLA_REFERENCE_ROOT)
 
 Imports the reference's own RandomFourierFeatures, OrthogonalRandomFeatures,
 LearnablePositiveMap (ultra_rwka/kernels/feature_maps.py), GateNet and
@@ -115,4 +115,9 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    from oracle.build_ref import REF_ENV, reference_root
+
+    root = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if root is None:
+        sys.exit(f"usage: python {sys.argv[0]} REFERENCE_ROOT (or set {REF_ENV})")
+    main(root)

@@ -99,6 +99,11 @@ def test_argument_validation_without_device():
     assert rc == 2 and b"scratch" in lib.fakla_last_error()
     rc = lib.fakla_decode_noalloc(p, p, p, None, p, None, p, p, p, 0, 1, 1, 1, 1, 1, None)
     assert rc == 1
+    # ... and it reports the argument error of an oversized call before its scratch limit
+    rc = lib.fakla_decode_noalloc(None, p, p, None, p, None, p, p, p, N, H * M, H, M, M, 1, None)
+    assert rc == 1 and b"non-NULL" in lib.fakla_last_error()
+    rc = lib.fakla_decode_noalloc(p, p, p, None, p, None, p, p, p, N, H * 512, H, 512, M, 1, None)
+    assert rc == 2 and b"head dims" in lib.fakla_last_error()
 
 
 def test_workspace_queries():

@@ -163,3 +163,22 @@ def test_phi_oracle_matches_torch():
     exp = torch.nn.functional.elu(x @ W.T + b) + 1.0
     got = O.phi(x.numpy(), W.numpy(), b.numpy())
     assert rel_l2(got, exp.numpy()) < 1e-14
+
+
+def test_oracle_rejects_head_dims_beyond_its_limit():
+    """The C restatement returns an error (and writes nothing) for head dims
+    above 256 instead of leaving the outputs unset."""
+    import ctypes
+
+    lib = O._load()
+    for fn, dt, p in ((lib.fakla_oracle_attention_f64, np.float64, ctypes.c_double),
+                      (lib.fakla_oracle_attention_f32, np.float32, ctypes.c_float)):
+        q = np.zeros((1, 1, 1, 300), dt)
+        v = np.zeros((1, 1, 1, 8), dt)
+        out = np.full((1, 1, 1, 8), 7, dt)
+        ptr = lambda a: a.ctypes.data_as(ctypes.POINTER(p))  # noqa: E731
+        rc = fn(ptr(q), ptr(q), ptr(v), None, ptr(out), None, None, None, None, 1, 1, 1, 300, 8)
+        assert rc == -1
+        assert (out == 7).all()
+    with pytest.raises(ValueError):
+        O.attention(np.zeros((1, 1, 1, 300)), np.zeros((1, 1, 1, 300)), np.zeros((1, 1, 1, 8)))

@@ -90,3 +90,37 @@ def test_noalloc_decode_rejects_oversized_step(cuda):
     assert b"scratch" in L.fakla_last_error()
     torch.cuda.synchronize()
     assert not out.any()
+
+
+def test_noalloc_decode_full_shape_against_oracle(cuda):
+    """The decode shape (batch 256, H=32, LearnablePositiveMap(4096 -> 4096),
+    bf16) once against the oracle itself rather than against fakla_decode, so
+    an error common to both entry points would not pass unseen."""
+    from oracle import fakla_oracle as O
+
+    L = _lib.lib()
+    N, H, D = 256, 32, 128
+    in_dim = H * D
+    g = torch.Generator(device=cuda).manual_seed(43)
+    W, b = lpm_params(in_dim, H * D, seed=44, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    S = torch.randn(N, H, D, D, generator=g, device=cuda) * 0.02
+    z = torch.rand(N, H, D, generator=g, device=cuda) + 0.5
+    q = (torch.randn(N, in_dim, generator=g, device=cuda) / math.sqrt(D)).bfloat16()
+    k = (torch.randn(N, in_dim, generator=g, device=cuda) / math.sqrt(D)).bfloat16()
+    v = (torch.randn(N, H, D, generator=g, device=cuda) / math.sqrt(D)).bfloat16()
+    idx = torch.tensor([0, 77, 128, 255], device=cuda)
+    S0, z0 = to_np(S[idx]).astype(np.float64), to_np(z[idx]).astype(np.float64)
+    out = torch.empty(N, H, D, device=cuda, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.fakla_decode_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), None, W.data_ptr(), b.data_ptr(),
+                                      out.data_ptr(), S.data_ptr(), z.data_ptr(), N, in_dim, H, D, D,
+                                      _lib.FAKLA_BF16, stream))
+    _lib.check(L.fakla_device_status(stream))
+    pq = O.phi(to_np(q[idx]), to_np(W), to_np(b)).reshape(len(idx), H, D)
+    pk = O.phi(to_np(k[idx]), to_np(W), to_np(b)).reshape(len(idx), H, D)
+    eo, eS, ez = O.decode_step(pq, pk, to_np(v[idx]), S0, z0)
+    got = to_np(out[idx])
+    assert rel_l2(got, eo) < BF16_REL_L2
+    assert np.abs(got - eo).max() < BF16_MAX_ABS
+    assert rel_l2(to_np(S[idx]), eS) < BF16_REL_L2 and rel_l2(to_np(z[idx]), ez) < BF16_REL_L2
