@@ -21,6 +21,49 @@ __device__ __forceinline__ void report_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Programmatic dependent launch (PDL). A kernel launched by launch_chained()
+// may begin while the kernel before it on the stream is still running (on SMs
+// that kernel has left): it sets up its shared memory, barriers and tensor
+// memory, then griddep_wait() blocks until that kernel has completed and its
+// memory is visible. Every thread calls it before its first global-memory
+// access. griddep_launch_dependents() (after the wait) lets the next chained
+// kernel be scheduled. For a kernel launched without the attribute both
+// return at once.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// cudaLaunchKernelEx with programmatic dependent launch allowed and, when
+// cluster_x > 1, clusters of cluster_x CTAs. Kernels launched this way call
+// griddep_wait() before touching global memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+#ifndef FAKLA_NO_PDL
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+#endif
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // phi activation: elu(x) + 1 = x + 1 for x > 0, exp(x) for x <= 0.
 // (F.elu(x) + 1.0 with alpha = 1, ultra_rwka/kernels/feature_maps.py:248.)
 __device__ __forceinline__ float elu_plus_one(float x) {

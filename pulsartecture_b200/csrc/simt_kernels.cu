@@ -327,6 +327,8 @@ __global__ void __launch_bounds__(256) decode_kernel(
   float* part = vv + dv4;   // [RPP][Dv]
   __shared__ float den_part[8];
 
+  griddep_wait();  // phi(q), phi(k) come from the feature-map launch before this one
+  griddep_launch_dependents();
   const int64_t bh = blockIdx.x;
   const int tid = threadIdx.x;
   const int TPR = Dv / VEC;
@@ -805,16 +807,15 @@ static cudaError_t launch_decode_t(const void* q, const void* k, const void* v,
     cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, 4>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    decode_kernel<T, 4><<<(unsigned)NH, 256, smem, stream>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
+    return launch_chained(decode_kernel<T, 4>, dim3((unsigned)NH), dim3(256), smem, stream, 1u, (const T*)q,
+                          (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
   } else {
     cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, 1>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    decode_kernel<T, 1><<<(unsigned)NH, 256, smem, stream>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
+    return launch_chained(decode_kernel<T, 1>, dim3((unsigned)NH), dim3(256), smem, stream, 1u, (const T*)q,
+                          (const T*)k, (const T*)v, (const T*)temp, (T*)out, S, z, (int)Df, (int)Dv);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v,

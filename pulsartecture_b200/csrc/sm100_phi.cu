@@ -30,6 +30,12 @@
 // (6 stages of 32 KB), so each SM moves a third fewer operand bytes per FLOP
 // through L2 and shared memory. Rank 0's commits arrive on both CTAs'
 // barriers; each CTA runs the epilogue of its own 128 rows from its own TMEM.
+//
+// A persistent grid gives every pair the tiles tile0, tile0 + pairs, ...; when
+// the tile count leaves a last wave less than half full (e.g. 256 tiles on 74
+// pairs: 3 waves + 34 tiles), those last tiles run as two 256x128 halves each
+// (N=128 MMAs, a W map with a 64-row box), so the tail takes half a tile's time
+// on twice as many pairs instead of a whole tile's time on a few.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -89,6 +95,7 @@ struct PhiArgs {
   int m;                       // features per head (temperature index = (col - tcol0) / m)
   int ident_from;              // columns >= ident_from skip the activation (N: none)
   int tcol0, tcol1;            // temperature applies to columns [tcol0, tcol1)
+  int n_full;                  // tiles [0, n_full) run whole, the rest as two column halves
   int* status;
 };
 
@@ -99,8 +106,9 @@ struct PhiArgs {
 template <int ACT, int BNT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC0,
-    const __grid_constant__ CUtensorMap tmC1, const PhiArgs args) {
+    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBh,
+    const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
+    const PhiArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -132,6 +140,26 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   const int tiles_per_set = row_tiles * col_tiles;
   const int total_tiles = tiles_per_set * args.nsets;
   const int kblocks = args.K / BK;
+  // work units: whole tiles [0, n_full), then each remaining tile as two
+  // halves of BNT / 2 columns (CTA pairs only; the host passes n_full =
+  // total_tiles otherwise)
+  const int n_full = args.n_full;
+  const int total_units = n_full + 2 * (total_tiles - n_full);
+  struct Unit {
+    int set, r;   // row set and tile within it
+    bool whole;
+    int coff;     // column offset of the unit within its tile (0 or BNT / 2)
+  };
+  auto unit_at = [&](int u) {
+    Unit t;
+    const bool whole = u < n_full;
+    const int tile = whole ? u : n_full + ((u - n_full) >> 1);
+    t.set = tile / tiles_per_set;
+    t.r = tile % tiles_per_set;
+    t.whole = whole;
+    t.coff = whole ? 0 : ((u - n_full) & 1) * (BNT / 2);
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -148,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     tma_prefetch_desc(&tmA0);
     tma_prefetch_desc(&tmA1);
     tma_prefetch_desc(&tmB);
+    if (n_full < total_tiles) tma_prefetch_desc(&tmBh);
     tma_prefetch_desc(&tmC0);
     tma_prefetch_desc(&tmC1);
   }
@@ -166,6 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // set-up done: from here on the kernel reads inputs earlier work may write
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -177,12 +209,15 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       int stage = 0;
       uint32_t phase = 0;
       long it = 0;
-      for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
-        const int set = tile / tiles_per_set;
-        const int r = tile % tiles_per_set;
-        const int row0 = (r / col_tiles) * kTileRows + (int)rank * BM;
-        const int col0 = (r % col_tiles) * BNT + (int)rank * kBRowsT<BNT, PAIR>;
-        const CUtensorMap* mapA = set == 0 ? &tmA0 : &tmA1;
+      for (int u = tile0; u < total_units && !*abort_flag; u += tile_step) {
+        const Unit t = unit_at(u);
+        const int row0 = (t.r / col_tiles) * kTileRows + (int)rank * BM;
+        // this CTA's rows of the unit's W tile (all of them for a single CTA)
+        const int brows = t.whole ? kBRowsT<BNT, PAIR> : kBRowsT<BNT, PAIR> / 2;
+        const int col0 = (t.r % col_tiles) * BNT + t.coff + (int)rank * brows;
+        const CUtensorMap* mapA = t.set == 0 ? &tmA0 : &tmA1;
+        const CUtensorMap* mapB = t.whole ? &tmB : &tmBh;
+        const uint32_t stage_tx = (uint32_t)(kABytes + brows * BK * 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const bool free = rank == 0 ? mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)
                                       : mbar_wait_cluster(&empty[stage], phase ^ 1u, kWaitNs);
@@ -193,13 +228,13 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
           }
           if constexpr (PAIR) {
             const uint32_t fb = mapa_shared(&full[stage], 0);
-            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * stage_tx);
             tma_load_2d_pair(sA + stage * kABytes, mapA, fb, kb * BK, row0);
-            tma_load_2d_pair(sB + stage * kBBytes, &tmB, fb, kb * BK, col0);
+            tma_load_2d_pair(sB + stage * kBBytes, mapB, fb, kb * BK, col0);
           } else {
-            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            mbar_arrive_expect_tx(&full[stage], stage_tx);
             tma_load_2d(sA + stage * kABytes, mapA, &full[stage], kb * BK, row0);
-            tma_load_2d(sB + stage * kBBytes, &tmB, &full[stage], kb * BK, col0);
+            tma_load_2d(sB + stage * kBBytes, mapB, &full[stage], kb * BK, col0);
           }
           if (++stage == kStages) {
             stage = 0;
@@ -218,12 +253,14 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kTileRows, BNT, false, false);
+      constexpr uint32_t idesc_whole = idesc_bf16_f32(kTileRows, BNT, false, false);
+      constexpr uint32_t idesc_half = idesc_bf16_f32(kTileRows, BNT / 2, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
+      for (int u = tile0; u < total_units && !*abort_flag; u += tile_step) {
+        const uint32_t idesc = u < n_full ? idesc_whole : idesc_half;
         const bool drained = PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, kWaitNs)
                                   : mbar_wait(&tempty[acc], acc_phase ^ 1u, kWaitNs);
         if (!drained) {
@@ -291,13 +328,14 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     int acc = 0;
     uint32_t acc_phase = 0;
     bool stored = false;
-    for (int tile = tile0; tile < total_tiles && !*abort_flag; tile += tile_step) {
-      const int set = tile / tiles_per_set;
-      const int r = tile % tiles_per_set;
-      const int row0 = (r / col_tiles) * kTileRows + (int)rank * BM;  // this CTA's 128 rows
-      const int col0 = (r % col_tiles) * BNT + half * kWarpCols;
-      const CUtensorMap* mapC = set == 0 ? &tmC0 : &tmC1;
-      const __nv_bfloat16* temp = set == 0 ? args.temp0 : args.temp1;
+    for (int u = tile0; u < total_units && !*abort_flag; u += tile_step) {
+      const Unit t = unit_at(u);
+      // columns of this warp: half of the unit's (BNT or BNT / 2)
+      const int wcols = t.whole ? kWarpCols : kWarpCols / 2;
+      const int row0 = (t.r / col_tiles) * kTileRows + (int)rank * BM;  // this CTA's 128 rows
+      const int col0 = (t.r % col_tiles) * BNT + t.coff + half * wcols;
+      const CUtensorMap* mapC = t.set == 0 ? &tmC0 : &tmC1;
+      const __nv_bfloat16* temp = t.set == 0 ? args.temp0 : args.temp1;
       const int grow = row0 + 32 * q + lane;  // this thread's output row
       // Pair: rank 0's commit lands on both CTAs' `tfull`.
       const bool ready = rank == 0 ? mbar_wait(&tfull[acc], acc_phase, kWaitNs)
@@ -309,14 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       }
       tc_fence_after();
       const uint32_t t_row =
-          tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BNT + half * kWarpCols);
+          tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BNT + half * wcols);
+      const int nj = wcols / 64;
 #pragma unroll 1
-      for (int j = 0; j < kWarpCols / 64; ++j) {
+      for (int j = 0; j < nj; ++j) {
         uint32_t v0[32], v1[32];
         tmem_ld32(t_row + (uint32_t)(j * 64), v0);
         tmem_ld32(t_row + (uint32_t)(j * 64 + 32), v1);
         tmem_ld_wait();
-        if (j == kWarpCols / 64 - 1) {
+        if (j == nj - 1) {
           // this warp's share of the accumulator is in registers: release it
           tc_fence_before();
           __syncwarp();
@@ -504,46 +543,38 @@ static int tiling_bn(int tiling) { return tiling == kTile128 ? 128 : BN; }
 // rows of W per CTA per stage (the TMA box height of the W map)
 static int tiling_b_rows(int tiling) { return tiling == kTilePair ? BN / 2 : tiling_bn(tiling); }
 
+// Tensor maps of one launch: x rows of both row sets, W (box of a CTA's rows
+// of a whole tile, and of half a tile for the split tail), outputs.
+struct PhiMaps {
+  CUtensorMap A0, A1, B, Bh, C0, C1;
+};
+
+// Tiles that run whole: all but a last wave that would leave more than half
+// the pairs idle, which runs as twice as many half tiles instead.
+static int64_t whole_tiles(int64_t tiles, int tiling) {
+  if (tiling != kTilePair) return tiles;
+  const int64_t slots = pair_slots();
+  const int64_t pairs = tiles < slots ? tiles : slots;
+  if (pairs < 1) return tiles;
+  const int64_t rem = tiles % pairs;
+  return (rem == 0 || 2 * rem > pairs) ? tiles : tiles - rem;
+}
+
 template <int ACT, int BNT, bool PAIR>
-static cudaError_t launch_act_t(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
-                                const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
-                                int64_t tiles, cudaStream_t stream) {
+static cudaError_t launch_act_t(const PhiMaps& m, const PhiArgs& a, int64_t units, cudaStream_t stream) {
   const auto kern = phi_gemm_sm100_kernel<ACT, BNT, PAIR>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytesT<BNT, PAIR>);
   if (e != cudaSuccess) return e;
   if constexpr (PAIR) {
-    const int64_t pairs = tiles < pair_slots() ? tiles : pair_slots();
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3((unsigned)(2 * pairs));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytesT<BNT, PAIR>;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, mA0, mA1, mB, mC0, mC1, a);
+    const int64_t pairs = units < pair_slots() ? units : pair_slots();
+    return launch_chained(kern, dim3((unsigned)(2 * pairs)), dim3(kThreads), kSmemBytesT<BNT, PAIR>, stream,
+                          2u, m.A0, m.A1, m.B, m.Bh, m.C0, m.C1, a);
   } else {
     const int sms = fakla_sm_count();
-    const int grid = tiles < sms ? (int)tiles : sms;
-    kern<<<grid, kThreads, kSmemBytesT<BNT, PAIR>, stream>>>(mA0, mA1, mB, mC0, mC1, a);
-    return cudaGetLastError();
-  }
-}
-
-// `tiles`: the number of output tiles of the chosen shape (all row sets).
-template <int ACT>
-static cudaError_t launch_act(const CUtensorMap& mA0, const CUtensorMap& mA1, const CUtensorMap& mB,
-                              const CUtensorMap& mC0, const CUtensorMap& mC1, const PhiArgs& a,
-                              int64_t tiles, int tiling, cudaStream_t stream) {
-  switch (tiling) {
-    case kTilePair: return launch_act_t<ACT, BN, true>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
-    case kTile128: return launch_act_t<ACT, 128, false>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
-    default: return launch_act_t<ACT, BN, false>(mA0, mA1, mB, mC0, mC1, a, tiles, stream);
+    const int grid = units < sms ? (int)units : sms;
+    return launch_chained(kern, dim3((unsigned)grid), dim3(kThreads), kSmemBytesT<BNT, PAIR>, stream, 1u,
+                          m.A0, m.A1, m.B, m.Bh, m.C0, m.C1, a);
   }
 }
 
@@ -552,23 +583,45 @@ static int64_t tile_count(int64_t rows, int64_t N, int nsets, int tiling) {
   return ((rows + tile_rows - 1) / tile_rows) * (N / tiling_bn(tiling)) * nsets;
 }
 
+// Fills a.n_full for the chosen tiling and launches.
+template <int ACT>
+static cudaError_t launch_act(const PhiMaps& m, PhiArgs a, int64_t rows, int64_t N, int tiling,
+                              cudaStream_t stream) {
+  const int64_t tiles = tile_count(rows, N, a.nsets, tiling);
+  const int64_t whole = whole_tiles(tiles, tiling);
+  a.n_full = (int)whole;
+  const int64_t units = whole + 2 * (tiles - whole);
+  switch (tiling) {
+    case kTilePair: return launch_act_t<ACT, BN, true>(m, a, units, stream);
+    case kTile128: return launch_act_t<ACT, 128, false>(m, a, units, stream);
+    default: return launch_act_t<ACT, BN, false>(m, a, units, stream);
+  }
+}
+
+// W maps: a CTA's rows of a whole tile and of a half tile (the half-tile map
+// is only read by the split tail of CTA-pair launches).
+static bool make_w_maps(PhiMaps* m, const void* W, int64_t K, int64_t N, int tiling) {
+  const uint32_t brows = (uint32_t)tiling_b_rows(tiling);
+  return make_map_2d(&m->B, W, (uint64_t)K, (uint64_t)N, BK, brows) &&
+         make_map_2d(&m->Bh, W, (uint64_t)K, (uint64_t)N, BK, tiling == kTilePair ? brows / 2 : brows);
+}
+
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
                              const void* temp0, const void* temp1, void* out0, void* out1,
                              int64_t rows, int64_t K, int64_t N, int64_t heads, int act,
                              float scale, cudaStream_t stream, int* status, bool* encoded) {
-  CUtensorMap mA0, mA1, mB, mC0, mC1;
+  PhiMaps m;
   const int nsets = x1 != nullptr ? 2 : 1;
   const int tiling = pick_tiling(rows, N, nsets);
   const uint64_t out_cols = (uint64_t)N * (act == FAKLA_ACT_COSSIN ? 2 : 1);
-  bool ok = make_map_2d(&mA0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-            make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)tiling_b_rows(tiling)) &&
-            make_map_2d(&mC0, out0, out_cols, (uint64_t)rows, 64, 32);
+  bool ok = make_map_2d(&m.A0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) && make_w_maps(&m, W, K, N, tiling) &&
+            make_map_2d(&m.C0, out0, out_cols, (uint64_t)rows, 64, 32);
   if (ok && nsets == 2)
-    ok = make_map_2d(&mA1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-         make_map_2d(&mC1, out1, out_cols, (uint64_t)rows, 64, 32);
+    ok = make_map_2d(&m.A1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
+         make_map_2d(&m.C1, out1, out_cols, (uint64_t)rows, 64, 32);
   else {
-    mA1 = mA0;
-    mC1 = mC0;
+    m.A1 = m.A0;
+    m.C1 = m.C0;
   }
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
@@ -587,16 +640,15 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   a.tcol0 = 0;
   a.tcol1 = (int)N;
   a.status = status;
-  const int64_t tiles = tile_count(rows, N, nsets, tiling);
   switch (act) {
-    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
-    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(mA0, mA1, mB, mC0, mC1, a, tiles, tiling, stream);
+    case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_RELU: return launch_act<FAKLA_ACT_RELU>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_SOFTPLUS: return launch_act<FAKLA_ACT_SOFTPLUS>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_GELU: return launch_act<FAKLA_ACT_GELU>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_IDENTITY: return launch_act<FAKLA_ACT_IDENTITY>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_SIGMOID: return launch_act<FAKLA_ACT_SIGMOID>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_ABS: return launch_act<FAKLA_ACT_ABS>(m, a, rows, N, tiling, stream);
+    case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(m, a, rows, N, tiling, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -613,10 +665,11 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
                              int64_t heads, cudaStream_t stream, int* status, bool* encoded) {
   const int64_t N = 2 * feat + vdim;
   const int tiling = pick_tiling(rows, N, 1);
-  CUtensorMap mA, mB, mC;
-  const bool ok = make_map_2d(&mA, x, (uint64_t)K, (uint64_t)rows, BK, BM) &&
-                  make_map_2d(&mB, W, (uint64_t)K, (uint64_t)N, BK, (uint32_t)tiling_b_rows(tiling)) &&
-                  make_map_2d(&mC, out, (uint64_t)N, (uint64_t)rows, 64, 32);
+  PhiMaps m;
+  const bool ok = make_map_2d(&m.A0, x, (uint64_t)K, (uint64_t)rows, BK, BM) && make_w_maps(&m, W, K, N, tiling) &&
+                  make_map_2d(&m.C0, out, (uint64_t)N, (uint64_t)rows, 64, 32);
+  m.A1 = m.A0;
+  m.C1 = m.C0;
   *encoded = ok;
   if (!ok) return cudaErrorInvalidValue;
   PhiArgs a;
@@ -634,7 +687,7 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
   a.tcol0 = (int)feat;
   a.tcol1 = (int)(2 * feat);
   a.status = status;
-  return launch_act<FAKLA_ACT_ELU1>(mA, mA, mB, mC, mC, a, tile_count(rows, N, 1, tiling), tiling, stream);
+  return launch_act<FAKLA_ACT_ELU1>(m, a, rows, N, tiling, stream);
 }
 
 }  // namespace fakla

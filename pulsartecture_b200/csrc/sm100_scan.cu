@@ -540,6 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       reinterpret_cast<uint4*>(base)[o % kPer] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  // set-up of shared memory done: from here on the kernel reads inputs
+  // earlier work may write
+  griddep_wait();
+  griddep_launch_dependents();
   // kScanRowAdd's centring vector, read by the output warps: m[0:64] in rows
   // 6-7 of M0, m[64:128] in rows 6-7 of M1 (zero without centring, so that
   // sigma * m is 0 whatever those rows held before)
@@ -1236,6 +1240,8 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   constexpr uint32_t kDColS = 0, kDColZ = 128;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1354,11 +1360,15 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
 
 // Record 0 of each sequence <- the caller's initial state (or 0); record g <-
 // record g-1 + the segment sum stored in record g. One thread per float4 of
-// a record, sequential over the G records (coalesced across threads).
+// a record (coalesced across threads), running over the G records with the
+// loads of 8 records in flight at once: the kernel is latency-bound, and one
+// dependent load per record cost a round trip each.
 __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const float* z_in, int G,
                                    int state_in, int hd) {
   constexpr int kS4 = D * D / 4;
   constexpr int kRec4 = (int)(kStateFloats / 4);
+  griddep_wait();
+  griddep_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= kRec4) return;
   const int64_t bh = blockIdx.y;
@@ -1379,13 +1389,22 @@ __global__ void scan_prefix_kernel(float* seg_init, const float* S_in, const flo
     }
   }
   rec[i] = acc;
-  for (int g = 1; g < G; ++g) {
-    const float4 d = rec[(int64_t)g * kRec4 + i];
-    acc.x += d.x;
-    acc.y += d.y;
-    acc.z += d.z;
-    acc.w += d.w;
-    rec[(int64_t)g * kRec4 + i] = acc;
+  constexpr int kBatch = 8;
+  for (int g0 = 1; g0 < G; g0 += kBatch) {
+    float4 d[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (g0 + j < G) d[j] = rec[(int64_t)(g0 + j) * kRec4 + i];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (g0 + j < G) {
+        acc.x += d[j].x;
+        acc.y += d[j].y;
+        acc.z += d[j].z;
+        acc.w += d[j].w;
+        rec[(int64_t)(g0 + j) * kRec4 + i] = acc;
+      }
+    }
   }
 }
 
@@ -1438,8 +1457,8 @@ static cudaError_t launch_main(const CUtensorMap& mQ, const CUtensorMap& mK, con
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  scan_sm100_kernel<MODE><<<(unsigned)ctas, kThreads, kSmemBytes, stream>>>(mQ, mK, mV, mO, mR, a);
-  return cudaGetLastError();
+  return launch_chained(scan_sm100_kernel<MODE>, dim3((unsigned)ctas), dim3(kThreads), kSmemBytes, stream, 1u,
+                        mQ, mK, mV, mO, mR, a);
 }
 
 static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v, const void* temp,
@@ -1496,11 +1515,13 @@ static cudaError_t launch_scan_impl(const void* q, const void* k, const void* v,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kDSmemBytes);
     if (e != cudaSuccess) return e;
-    scan_delta_sm100_kernel<<<(unsigned)(B * H * (G - 1)), kDThreads, kDSmemBytes, stream>>>(mK, mV, d);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = launch_chained(scan_delta_sm100_kernel, dim3((unsigned)(B * H * (G - 1))), dim3(kDThreads), kDSmemBytes,
+                       stream, 1u, mK, mV, d);
+    if (e != cudaSuccess) return e;
     const dim3 pgrid((unsigned)((kStateFloats / 4 + 255) / 256), (unsigned)(B * H));
-    scan_prefix_kernel<<<pgrid, 256, 0, stream>>>(seg_init, S, z, G, state_in ? 1 : 0, (int)hd);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = launch_chained(scan_prefix_kernel, pgrid, dim3(256), 0, stream, 1u, seg_init, (const float*)S,
+                       (const float*)z, G, state_in ? 1 : 0, (int)hd);
+    if (e != cudaSuccess) return e;
   }
 
   ScanArgs a;

@@ -83,6 +83,48 @@ def test_phi_bf16_tensor_core(cuda, rows, K, N, heads, use_bias, use_temp):
     assert np.all(np.abs(g - exp) <= 2.0 ** -8 * np.abs(exp) + 1e-4)
 
 
+@pytest.mark.parametrize("rows,nsets", [(8192, 1), (4096, 2)])
+def test_phi_split_tail_against_oracle(cuda, rows, nsets):
+    """256 tiles of 256 x 256 on the CTA pairs leave a last wave a third full:
+    those tiles run as two 256 x 128 halves each (the per-GPU feature map of
+    an 8-way split of B=8, H=16, T=4096: 2 x 4096 rows x 2048 -> 2048). The
+    rows of the tail (the last 1280 rows of the last row set) and some of the
+    first are checked against the oracle, with the k-side temperature."""
+    from pulsartecture_b200 import _lib
+
+    L = _lib.lib()
+    K = N = 2048
+    heads = 16
+    x = _normal((nsets, rows, K), 30, cuda, torch.bfloat16, 1 / np.sqrt(128))
+    W, b = lpm_params(K, N, seed=31, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    temp = _phi_like((rows, heads), 32, cuda, torch.bfloat16)
+    out = torch.empty(nsets, rows, N, device=cuda, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    if nsets == 1:
+        _lib.check(L.fakla_phi(x.data_ptr(), W.data_ptr(), b.data_ptr(), temp.data_ptr(), out.data_ptr(), rows, K,
+                               N, heads, _lib.FAKLA_BF16, stream))
+    else:
+        # both row sets in one launch, as the prefill runs phi(q) and phi(k) * temp
+        B_, T_ = 1, rows
+        v = torch.zeros(B_, T_, heads, N // heads, device=cuda, dtype=torch.bfloat16)
+        o = torch.empty_like(v)
+        wsb = L.fakla_prefill_workspace_bytes(B_, T_, K, heads, N // heads, N // heads, _lib.FAKLA_BF16)
+        ws = torch.empty(wsb, device=cuda, dtype=torch.uint8)
+        _lib.check(L.fakla_prefill(x[0].data_ptr(), x[1].data_ptr(), v.data_ptr(), temp.data_ptr(), W.data_ptr(),
+                                   b.data_ptr(), o.data_ptr(), None, None, B_, T_, K, heads, N // heads, N // heads,
+                                   _lib.FAKLA_BF16, 0, ws.data_ptr(), wsb, stream))
+        one = rows * N * 2
+        out.view(-1).view(torch.uint8).copy_(ws[:2 * one])
+    _lib.check(L.fakla_device_status(stream))
+    sample = np.r_[0:64, rows - 1280:rows:7]
+    for s in range(nsets):
+        tp = to_np(temp)[sample] if s == nsets - 1 else None
+        exp = O.phi(to_np(x[s])[sample], to_np(W), to_np(b), tp, heads)
+        g = to_np(out[s])[sample]
+        assert np.all(np.abs(g - exp) <= 2.0 ** -8 * np.abs(exp) + 1e-4), s
+
+
 def test_phi_f32(cuda):
     from pulsartecture_b200.backend.interface import phi_map
 
