@@ -182,6 +182,31 @@ int fakla_activation_backward(const void* pre, const void* dy, void* dpre, int64
                               int64_t n, int act, float scale, int dtype, void* stream);
 
 /*
+ * fakla_linear_backward -- gradients of one linear layer y = x W^T + b from
+ * dpre = dL/dy (for a feature map: the output of fakla_phi_backward or
+ * fakla_activation_backward):
+ *   dx = dpre W  (rows, in_dim)    dW = dpre^T x  (n_out, in_dim)    db = sum over rows of dpre  (n_out)
+ *
+ * Reference: none (no backward in the reference); the input, weight and bias
+ * gradients of the nn.Linear inside LearnablePositiveMap (ultra_rwka/kernels/
+ * feature_maps.py:224-232), GateNet and TemperatureFunction, and of the
+ * projection of RandomFourierFeatures / OrthogonalRandomFeatures.
+ *   x : (rows, in_dim)   W : (n_out, in_dim)   dpre : (rows, n_out)
+ *   dx, dW, db : written when non-NULL (x may be NULL without dW, W without dx)
+ * db needs a workspace of fakla_linear_backward_workspace_bytes() (fp32
+ * partial sums, added in a fixed order); dx and dW need none. bf16 with
+ * in_dim % 128 == 0, n_out % 8 == 0 and 16-byte aligned pointers runs both
+ * products on the tensor cores (fp32 accumulation); other shapes and fp32 run
+ * on the CUDA cores.
+ */
+int fakla_linear_backward(const void* x, const void* W, const void* dpre, void* dx, void* dW,
+                          void* db, int64_t rows, int64_t in_dim, int64_t n_out, int dtype,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+size_t fakla_linear_backward_workspace_bytes(int64_t rows, int64_t in_dim, int64_t n_out,
+                                             int dtype);
+
+/*
  * fakla_mix_features_backward -- gradients of fakla_mix_features.
  * With w = softmax(logits) (rounded to dtype as in the forward):
  *   dfeats[i] = w_i dout,  dlogits_i = w_i (dw_i - sum_j w_j dw_j),  dw_i = dout . feats[i]

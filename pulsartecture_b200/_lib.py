@@ -58,6 +58,8 @@ SIGNATURES = {
     "fakla_attention_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "fakla_phi_backward": (_int, [_p, _p, _p, _i64, _int, _p]),
     "fakla_activation_backward": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_float, _int, _p]),
+    "fakla_linear_backward": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _sz, _p]),
+    "fakla_linear_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "fakla_mix_features_backward": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "fakla_feature_map": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, ctypes.c_float, _int, _p]),
     "fakla_mix_features": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),

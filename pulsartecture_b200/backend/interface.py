@@ -610,10 +610,37 @@ class _AttentionFn(torch.autograd.Function):
         return dq, dk, dv, dtemp, dS0, dz0
 
 
+def _linear_backward(x, W, dpre, want_dx: bool, want_dW: bool, want_db: bool):
+    """dx = dpre W, dW = dpre^T x, db = sum_rows dpre of one linear layer
+    (fakla_linear_backward: tensor-core GEMMs for bf16, CUDA cores otherwise)."""
+    x = None if x is None else x.contiguous()
+    W, dpre = W.contiguous(), dpre.contiguous()
+    rows, n_out = dpre.shape
+    in_dim = W.shape[1]
+    dev = dpre.device
+    dx = torch.empty(rows, in_dim, device=dev, dtype=dpre.dtype) if want_dx else None
+    dW = torch.empty(n_out, in_dim, device=dev, dtype=dpre.dtype) if want_dW else None
+    db = torch.empty(n_out, device=dev, dtype=dpre.dtype) if want_db else None
+    if not (want_dx or want_dW or want_db) or rows == 0:
+        if db is not None:
+            db.zero_()
+        if dW is not None:
+            dW.zero_()
+        return dx, dW, db
+    L = _lib.lib()
+    code = _dtype_code(dpre)
+    with torch.cuda.device(dev):
+        ws_bytes = L.fakla_linear_backward_workspace_bytes(rows, in_dim, n_out, code) if want_db else 0
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+        _lib.check(L.fakla_linear_backward(_ptr(x), _ptr(W), _ptr(dpre), _ptr(dx), _ptr(dW), _ptr(db), rows,
+                                           in_dim, n_out, code, _ptr(ws), ws_bytes, _stream(dev)))
+    return dx, dW, db
+
+
 class _PhiFn(torch.autograd.Function):
     """phi(x) = elu(x W^T + b) + 1 with gradients: forward fakla_phi; backward
-    fakla_phi_backward (dpre = dphi * min(phi, 1)), then the two weight/input
-    GEMMs dx = dpre W, dW = dpre^T x (cuBLAS) and db = sum_rows dpre."""
+    fakla_phi_backward (dpre = dphi * min(phi, 1)), then fakla_linear_backward
+    (dx = dpre W, dW = dpre^T x, db = sum_rows dpre)."""
 
     @staticmethod
     def forward(ctx, x, W, b):
@@ -639,17 +666,15 @@ class _PhiFn(torch.autograd.Function):
         with torch.cuda.device(dev):
             _lib.check(L.fakla_phi_backward(_ptr(phi), _ptr(dphi), _ptr(dpre), phi.numel(), _dtype_code(phi),
                                             _stream(dev)))
-        dx = dpre @ W if ctx.needs_input_grad[0] else None
-        dW = dpre.t() @ x if ctx.needs_input_grad[1] else None
-        db = dpre.sum(0) if ctx.has_bias and ctx.needs_input_grad[2] else None
-        return dx, dW, db
+        return _linear_backward(x, W, dpre, ctx.needs_input_grad[0], ctx.needs_input_grad[1],
+                                ctx.has_bias and ctx.needs_input_grad[2])
 
 
 class _FeatureMapFn(torch.autograd.Function):
     """act(x W^T + b) with gradients for every fakla_feature_map activation:
     the backward recomputes the pre-activation with one identity launch,
-    applies fakla_activation_backward, then dx = dpre W and dW = dpre^T x
-    (cuBLAS) and db = sum_rows dpre."""
+    applies fakla_activation_backward, then fakla_linear_backward (dx = dpre W,
+    dW = dpre^T x, db = sum_rows dpre)."""
 
     @staticmethod
     def forward(ctx, x, W, b, act, scale):
@@ -673,9 +698,8 @@ class _FeatureMapFn(torch.autograd.Function):
         with torch.cuda.device(dev):
             _lib.check(L.fakla_activation_backward(_ptr(pre), _ptr(dy), _ptr(dpre), rows, n, ACTIVATIONS[ctx.act],
                                                    ctx.scale, _dtype_code(pre), _stream(dev)))
-        dx = dpre @ W if ctx.needs_input_grad[0] else None
-        dW = dpre.t() @ x if ctx.needs_input_grad[1] else None
-        db = dpre.sum(0) if b is not None and ctx.needs_input_grad[2] else None
+        dx, dW, db = _linear_backward(x, W, dpre, ctx.needs_input_grad[0], ctx.needs_input_grad[1],
+                                      b is not None and ctx.needs_input_grad[2])
         return dx, dW, db, None, None
 
 

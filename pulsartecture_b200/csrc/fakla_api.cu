@@ -435,6 +435,68 @@ extern "C" int fakla_activation_backward(const void* pre, const void* dy, void* 
   return FAKLA_OK;
 }
 
+extern "C" size_t fakla_linear_backward_workspace_bytes(int64_t rows, int64_t in_dim, int64_t n_out,
+                                                        int dtype) {
+  (void)in_dim;
+  (void)dtype;
+  if (rows < 1 || n_out < 1) return 0;
+  return round_up(fakla::colsum_workspace_bytes(rows, n_out), 256);
+}
+
+extern "C" int fakla_linear_backward(const void* x, const void* W, const void* dpre, void* dx, void* dW,
+                                     void* db, int64_t rows, int64_t in_dim, int64_t n_out, int dtype,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!dpre) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "dpre must be non-NULL");
+  if ((dx && !W) || (dW && !x))
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "dx needs W and dW needs x");
+  if (rows < 1 || in_dim < 1 || n_out < 1)
+    return fakla_set_error(FAKLA_ERR_INVALID_ARG, "sizes must be positive");
+  if (db) {
+    const size_t need = fakla_linear_backward_workspace_bytes(rows, in_dim, n_out, dtype);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fakla_set_error(FAKLA_ERR_WORKSPACE, "the bias gradient needs %zu workspace bytes, got %zu", need,
+                             workspace == nullptr ? (size_t)0 : workspace_bytes);
+    if (((uintptr_t)workspace & 3u) != 0)
+      return fakla_set_error(FAKLA_ERR_ALIGNMENT, "workspace must be 4-byte aligned");
+  }
+  DeviceInfo* d = nullptr;
+  if ((rc = require_device(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // dx (rows, in_dim) = dpre (rows, n_out; K-major) W (n_out, in_dim; MN-major)
+  if (dx) {
+    cudaError_t e;
+    if (dtype == FAKLA_BF16 && fakla::gemm_sm100_supported(rows, in_dim, n_out, false, true) && aligned16(dpre) &&
+        aligned16(W) && aligned16(dx)) {
+      bool enc = false;
+      e = fakla::launch_gemm_sm100(dpre, false, W, true, dx, rows, in_dim, n_out, st, d->st(), &enc);
+      if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+    } else {
+      e = fakla::launch_gemm_strided(dtype, dpre, n_out, 1, W, 1, in_dim, dx, rows, in_dim, n_out, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "input gradient launch");
+  }
+  // dW (n_out, in_dim) = dpre^T (dpre stored (rows, n_out): MN-major) x (rows, in_dim: MN-major)
+  if (dW) {
+    cudaError_t e;
+    if (dtype == FAKLA_BF16 && fakla::gemm_sm100_supported(n_out, in_dim, rows, true, true) && aligned16(dpre) &&
+        aligned16(x) && aligned16(dW)) {
+      bool enc = false;
+      e = fakla::launch_gemm_sm100(dpre, true, x, true, dW, n_out, in_dim, rows, st, d->st(), &enc);
+      if (!enc) return fakla_set_error(FAKLA_ERR_INVALID_ARG, "TMA descriptor encoding failed");
+    } else {
+      e = fakla::launch_gemm_strided(dtype, dpre, 1, n_out, x, 1, in_dim, dW, n_out, in_dim, rows, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "weight gradient launch");
+  }
+  if (db) {
+    cudaError_t e = fakla::launch_colsum(dtype, dpre, db, (float*)workspace, rows, n_out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "bias gradient launch");
+  }
+  return FAKLA_OK;
+}
+
 extern "C" int fakla_mix_features_backward(const void* feats, const void* logits, const void* dout,
                                            void* dfeats, void* dlogits, int64_t rows,
                                            int64_t n_maps, int64_t feat_dim, int dtype,

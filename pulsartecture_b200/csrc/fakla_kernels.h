@@ -50,12 +50,28 @@ cudaError_t launch_mix_backward(int dtype, const void* feats, const void* logits
                                 void* dfeats, void* dlogits, int64_t rows, int64_t n_maps,
                                 int64_t F, cudaStream_t stream);
 
+// Linear-layer gradients on the CUDA cores: C (M, N) row-major =
+// sum_k A[m*sam + k*sak] B[n*sbn + k*sbk]; column sums of x (rows, n) through
+// colsum_workspace_bytes() of fp32 partial sums (deterministic order).
+cudaError_t launch_gemm_strided(int dtype, const void* A, int64_t sam, int64_t sak, const void* Bm, int64_t sbn,
+                                int64_t sbk, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+size_t colsum_workspace_bytes(int64_t rows, int64_t n);
+cudaError_t launch_colsum(int dtype, const void* x, void* out, float* partial, int64_t rows, int64_t n,
+                          cudaStream_t stream);
+
 // Tensor-core kernels (sm100_phi.cu, sm100_scan.cu); bf16 only.
 bool phi_sm100_supported(int64_t rows, int64_t K, int64_t N, int64_t heads);
 cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, const void* bias,
                              const void* temp0, const void* temp1, void* out0, void* out1,
                              int64_t rows, int64_t K, int64_t N, int64_t heads, int act,
                              float scale, cudaStream_t stream, int* status, bool* encoded);
+// D (M, N) row-major bf16 = A B^T with fp32 accumulation on the tensor cores:
+// A is (M, K) row-major, or (K, M) row-major when a_mn; B is (N, K) row-major,
+// or (K, N) row-major when b_mn. N % 128 == 0; M and K are free (a ragged K
+// reads zeros past its end).
+bool gemm_sm100_supported(int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn);
+cudaError_t launch_gemm_sm100(const void* A, bool a_mn, const void* B, bool b_mn, void* D, int64_t M,
+                              int64_t N, int64_t K, cudaStream_t stream, int* status, bool* encoded);
 // Df = Dv = 128, or 64 (the forward only: run in the 128-wide tiles with the
 // second half held at zero).
 bool scan_sm100_supported(int64_t B, int64_t T, int64_t H, int64_t Df, int64_t Dv);

@@ -818,6 +818,129 @@ static cudaError_t launch_decode_t(const void* q, const void* k, const void* v,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Linear-layer gradients on the CUDA cores (fp32, and bf16 shapes outside the
+// tensor-core set): a tiled GEMM over strided operands,
+//   C[m, n] = sum_k A[m sam + k sak] B[n sbn + k sbk]   (C row-major, fp32 accumulation)
+// which covers dx = dpre W and dW = dpre^T x, and a column sum for the bias.
+// ---------------------------------------------------------------------------
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_strided_simt_kernel(
+    const T* __restrict__ A, int64_t sam, int64_t sak, const T* __restrict__ Bm, int64_t sbn,
+    int64_t sbk, T* __restrict__ C, int64_t M, int64_t N, int64_t K) {
+  __shared__ float as[kPhiK][kPhiTile + 4];
+  __shared__ float bs[kPhiK][kPhiTile + 4];
+  const int tid = threadIdx.x;
+  const int64_t m0 = (int64_t)blockIdx.y * kPhiTile;
+  const int64_t n0 = (int64_t)blockIdx.x * kPhiTile;
+  const int tr = tid / 16, tc = tid % 16;
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += kPhiK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      // consecutive threads walk k when the operand is k-contiguous, else the
+      // row index, so that either layout reads whole sectors
+      const bool ak = sak == 1, bk = sbk == 1;
+      const int ra = ak ? e / kPhiK : e % kPhiTile, ka = ak ? e % kPhiK : e / kPhiTile;
+      const int rb = bk ? e / kPhiK : e % kPhiTile, kb = bk ? e % kPhiK : e / kPhiTile;
+      const int64_t gm = m0 + ra, gka = k0 + ka, gn = n0 + rb, gkb = k0 + kb;
+      as[ka][ra] = (gm < M && gka < K) ? to_f32(A[gm * sam + gka * sak]) : 0.f;
+      bs[kb][rb] = (gn < N && gkb < K) ? to_f32(Bm[gn * sbn + gkb * sbk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kPhiK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = as[kk][tr * 4 + i];
+        b[i] = bs[kk][tc * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gm = m0 + tr * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gn = n0 + tc * 4 + j;
+      if (gn < N) C[gm * N + gn] = from_f32<T>(acc[i][j]);
+    }
+  }
+}
+
+constexpr int kColSumRows = 256;  // rows per partial sum of the column reduction
+
+// partial[c, n] = sum of rows [c * kColSumRows, (c + 1) * kColSumRows) of column n
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict__ x, float* __restrict__ partial,
+                                                             int64_t rows, int64_t n) {
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= n) return;
+  const int64_t r0 = (int64_t)blockIdx.y * kColSumRows;
+  const int64_t r1 = min(rows, r0 + kColSumRows);
+  float acc = 0.f;
+  for (int64_t r = r0; r < r1; ++r) acc += to_f32(x[r * n + col]);
+  partial[(int64_t)blockIdx.y * n + col] = acc;
+}
+
+// out[n] = sum over the partial rows, in order (deterministic)
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ partial, T* __restrict__ out,
+                                                           int64_t chunks, int64_t n) {
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= n) return;
+  float acc = 0.f;
+  for (int64_t c = 0; c < chunks; ++c) acc += partial[c * n + col];
+  out[col] = from_f32<T>(acc);
+}
+
+template <typename T>
+cudaError_t launch_gemm_strided_t(const void* A, int64_t sam, int64_t sak, const void* Bm, int64_t sbn, int64_t sbk,
+                                  void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  const dim3 grid((unsigned)((N + kPhiTile - 1) / kPhiTile), (unsigned)((M + kPhiTile - 1) / kPhiTile));
+  gemm_strided_simt_kernel<T><<<grid, 256, 0, stream>>>((const T*)A, sam, sak, (const T*)Bm, sbn, sbk, (T*)C, M, N,
+                                                        K);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_colsum_t(const void* x, void* out, float* partial, int64_t rows, int64_t n, cudaStream_t stream) {
+  const int64_t chunks = (rows + kColSumRows - 1) / kColSumRows;
+  const unsigned gx = (unsigned)((n + 255) / 256);
+  colsum_partial_kernel<T><<<dim3(gx, (unsigned)chunks), 256, 0, stream>>>((const T*)x, partial, rows, n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  colsum_final_kernel<T><<<gx, 256, 0, stream>>>(partial, (T*)out, chunks, n);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_gemm_strided(int dtype, const void* A, int64_t sam, int64_t sak, const void* Bm, int64_t sbn,
+                                int64_t sbk, void* C, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (dtype == FAKLA_BF16)
+    return launch_gemm_strided_t<__nv_bfloat16>(A, sam, sak, Bm, sbn, sbk, C, M, N, K, stream);
+  return launch_gemm_strided_t<float>(A, sam, sak, Bm, sbn, sbk, C, M, N, K, stream);
+}
+
+size_t colsum_workspace_bytes(int64_t rows, int64_t n) {
+  return (size_t)((rows + kColSumRows - 1) / kColSumRows) * (size_t)n * sizeof(float);
+}
+
+cudaError_t launch_colsum(int dtype, const void* x, void* out, float* partial, int64_t rows, int64_t n,
+                          cudaStream_t stream) {
+  if (dtype == FAKLA_BF16) return launch_colsum_t<__nv_bfloat16>(x, out, partial, rows, n, stream);
+  return launch_colsum_t<float>(x, out, partial, rows, n, stream);
+}
+
 cudaError_t launch_decode(int dtype, const void* q, const void* k, const void* v,
                           const void* temp, void* out, float* S, float* z, int64_t NH,
                           int64_t Df, int64_t Dv, cudaStream_t stream) {

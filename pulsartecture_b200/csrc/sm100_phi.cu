@@ -103,7 +103,12 @@ struct PhiArgs {
 // 256 x BNT tile together with cta_group::2 MMAs (rank 0 issues them; each
 // CTA loads its 128 rows of x and half of the W tile and runs the epilogue of
 // its 128 rows), so each SM streams a third fewer operand bytes per FLOP.
-template <int ACT, int BNT, bool PAIR>
+// AMN / BMN: the A (x) / B (W) operand is stored MN-major, i.e. as (K, M) /
+// (K, N) row-major matrices (the transposed operands of a linear layer's
+// input and weight gradients); each stage then holds 64-row K slabs of 64-wide
+// MN atoms (kMnAtom bytes apart) loaded as 64 x 64 boxes.
+constexpr int kMnAtom = BK * 128;  // 8 KB: 64 K rows x 64 MN elements
+template <int ACT, int BNT, bool PAIR, bool AMN = false, bool BMN = false>
 __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBh,
@@ -114,7 +119,6 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
                                              ~uintptr_t(1023));
   constexpr int kStages = kStagesT<BNT, PAIR>;
   constexpr int kBBytes = kBBytesT<BNT, PAIR>;
-  constexpr int kStageBytes = kStageBytesT<BNT, PAIR>;
   constexpr uint32_t kTmemCols = kTmemColsT<BNT>;
   constexpr int kTileRows = PAIR ? 2 * BM : BM;
   uint8_t* sA = smem;                                  // kStages x 16 KB
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   const int col_tiles = args.N / BNT;
   const int tiles_per_set = row_tiles * col_tiles;
   const int total_tiles = tiles_per_set * args.nsets;
-  const int kblocks = args.K / BK;
+  const int kblocks = (args.K + BK - 1) / BK;  // a ragged last block reads zeros past K
   // work units: whole tiles [0, n_full), then each remaining tile as two
   // halves of BNT / 2 columns (CTA pairs only; the host passes n_full =
   // total_tiles otherwise)
@@ -226,15 +230,33 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             *abort_flag = 1;
             break;
           }
+          uint8_t* dA = sA + stage * kABytes;
+          uint8_t* dB = sB + stage * kBBytes;
           if constexpr (PAIR) {
             const uint32_t fb = mapa_shared(&full[stage], 0);
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * stage_tx);
-            tma_load_2d_pair(sA + stage * kABytes, mapA, fb, kb * BK, row0);
-            tma_load_2d_pair(sB + stage * kBBytes, mapB, fb, kb * BK, col0);
+            if constexpr (AMN) {
+              for (int a = 0; a < BM / 64; ++a) tma_load_2d_pair(dA + a * kMnAtom, mapA, fb, row0 + 64 * a, kb * BK);
+            } else {
+              tma_load_2d_pair(dA, mapA, fb, kb * BK, row0);
+            }
+            if constexpr (BMN) {
+              for (int a = 0; a < brows / 64; ++a) tma_load_2d_pair(dB + a * kMnAtom, mapB, fb, col0 + 64 * a, kb * BK);
+            } else {
+              tma_load_2d_pair(dB, mapB, fb, kb * BK, col0);
+            }
           } else {
             mbar_arrive_expect_tx(&full[stage], stage_tx);
-            tma_load_2d(sA + stage * kABytes, mapA, &full[stage], kb * BK, row0);
-            tma_load_2d(sB + stage * kBBytes, mapB, &full[stage], kb * BK, col0);
+            if constexpr (AMN) {
+              for (int a = 0; a < BM / 64; ++a) tma_load_2d(dA + a * kMnAtom, mapA, &full[stage], row0 + 64 * a, kb * BK);
+            } else {
+              tma_load_2d(dA, mapA, &full[stage], kb * BK, row0);
+            }
+            if constexpr (BMN) {
+              for (int a = 0; a < brows / 64; ++a) tma_load_2d(dB + a * kMnAtom, mapB, &full[stage], col0 + 64 * a, kb * BK);
+            } else {
+              tma_load_2d(dB, mapB, &full[stage], kb * BK, col0);
+            }
           }
           if (++stage == kStages) {
             stage = 0;
@@ -253,8 +275,13 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc_whole = idesc_bf16_f32(kTileRows, BNT, false, false);
-      constexpr uint32_t idesc_half = idesc_bf16_f32(kTileRows, BNT / 2, false, false);
+      constexpr uint32_t idesc_whole = idesc_bf16_f32(kTileRows, BNT, AMN, BMN);
+      constexpr uint32_t idesc_half = idesc_bf16_f32(kTileRows, BNT / 2, AMN, BMN);
+      // descriptor steps per 16-element K slice: 32 bytes inside a K-major
+      // atom row, 16 K rows (2048 bytes) of an MN-major atom; LBO = the MN
+      // atom stride for MN-major operands
+      constexpr uint64_t kStepA = AMN ? 2048 >> 4 : 32 >> 4;
+      constexpr uint64_t kStepB = BMN ? 2048 >> 4 : 32 >> 4;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -277,17 +304,14 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             break;
           }
           tc_fence_after();
-          const uint64_t da = smem_desc_sw128(smem_u32(sA + stage * kABytes), 16, 1024);
-          const uint64_t db = smem_desc_sw128(smem_u32(sB + stage * kBBytes), 16, 1024);
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + stage * kABytes), AMN ? kMnAtom : 16, 1024);
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + stage * kBBytes), BMN ? kMnAtom : 16, 1024);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // advance 16 bf16 = 32 bytes along K inside the 128-byte swizzle atom
             if constexpr (PAIR)
-              mma_ss_pair(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                          (kb | k) != 0 ? 1u : 0u);
+              mma_ss_pair(d_tmem, da + kStepA * k, db + kStepB * k, idesc, (kb | k) != 0 ? 1u : 0u);
             else
-              mma_ss(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+              mma_ss(d_tmem, da + kStepA * k, db + kStepB * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           if constexpr (PAIR)
             mma_commit_pair(&empty[stage]);
@@ -560,9 +584,9 @@ static int64_t whole_tiles(int64_t tiles, int tiling) {
   return (rem == 0 || 2 * rem > pairs) ? tiles : tiles - rem;
 }
 
-template <int ACT, int BNT, bool PAIR>
+template <int ACT, int BNT, bool PAIR, bool AMN = false, bool BMN = false>
 static cudaError_t launch_act_t(const PhiMaps& m, const PhiArgs& a, int64_t units, cudaStream_t stream) {
-  const auto kern = phi_gemm_sm100_kernel<ACT, BNT, PAIR>;
+  const auto kern = phi_gemm_sm100_kernel<ACT, BNT, PAIR, AMN, BMN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytesT<BNT, PAIR>);
   if (e != cudaSuccess) return e;
@@ -584,7 +608,7 @@ static int64_t tile_count(int64_t rows, int64_t N, int nsets, int tiling) {
 }
 
 // Fills a.n_full for the chosen tiling and launches.
-template <int ACT>
+template <int ACT, bool AMN = false, bool BMN = false>
 static cudaError_t launch_act(const PhiMaps& m, PhiArgs a, int64_t rows, int64_t N, int tiling,
                               cudaStream_t stream) {
   const int64_t tiles = tile_count(rows, N, a.nsets, tiling);
@@ -592,9 +616,9 @@ static cudaError_t launch_act(const PhiMaps& m, PhiArgs a, int64_t rows, int64_t
   a.n_full = (int)whole;
   const int64_t units = whole + 2 * (tiles - whole);
   switch (tiling) {
-    case kTilePair: return launch_act_t<ACT, BN, true>(m, a, units, stream);
-    case kTile128: return launch_act_t<ACT, 128, false>(m, a, units, stream);
-    default: return launch_act_t<ACT, BN, false>(m, a, units, stream);
+    case kTilePair: return launch_act_t<ACT, BN, true, AMN, BMN>(m, a, units, stream);
+    case kTile128: return launch_act_t<ACT, 128, false, AMN, BMN>(m, a, units, stream);
+    default: return launch_act_t<ACT, BN, false, AMN, BMN>(m, a, units, stream);
   }
 }
 
@@ -651,6 +675,64 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
     case FAKLA_ACT_COSSIN: return launch_act<FAKLA_ACT_COSSIN>(m, a, rows, N, tiling, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+bool gemm_sm100_supported(int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn) {
+  if (M < 1 || N < 128 || K < 1 || N % 128 != 0) return false;
+  if (M > (int64_t)INT32_MAX / 2 || N > (int64_t)INT32_MAX / 2 || K > (int64_t)INT32_MAX / 2) return false;
+  // row strides of the operands (16-byte multiples for TMA): K-major rows hold
+  // K elements, MN-major rows M or N
+  if (!a_mn && K % 8 != 0) return false;
+  if (a_mn && M % 8 != 0) return false;
+  // B's rows hold K (K-major) or N (MN-major) elements; N % 128 == 0 covers the
+  // latter. The innermost extent of every operand spans at least one 64-wide
+  // box (the boxes may run past the outer extents, which read as zeros).
+  if ((!a_mn || !b_mn) && K < 64) return false;
+  if (a_mn && M < 64) return false;
+  return true;
+}
+
+cudaError_t launch_gemm_sm100(const void* A, bool a_mn, const void* B, bool b_mn, void* D, int64_t M,
+                              int64_t N, int64_t K, cudaStream_t stream, int* status, bool* encoded) {
+  if (!b_mn && K % 8 != 0) {
+    *encoded = false;
+    return cudaErrorInvalidValue;
+  }
+  PhiMaps m;
+  const int tiling = pick_tiling(M, N, 1);
+  const uint32_t brows = (uint32_t)tiling_b_rows(tiling);
+  bool ok = a_mn ? make_map_2d(&m.A0, A, (uint64_t)M, (uint64_t)K, 64, BK)
+                 : make_map_2d(&m.A0, A, (uint64_t)K, (uint64_t)M, BK, BM);
+  if (b_mn)
+    ok = ok && make_map_2d(&m.B, B, (uint64_t)N, (uint64_t)K, 64, BK) &&
+         make_map_2d(&m.Bh, B, (uint64_t)N, (uint64_t)K, 64, BK);
+  else
+    ok = ok && make_map_2d(&m.B, B, (uint64_t)K, (uint64_t)N, BK, brows) &&
+         make_map_2d(&m.Bh, B, (uint64_t)K, (uint64_t)N, BK, tiling == kTilePair ? brows / 2 : brows);
+  ok = ok && make_map_2d(&m.C0, D, (uint64_t)N, (uint64_t)M, 64, 32);
+  *encoded = ok;
+  if (!ok) return cudaErrorInvalidValue;
+  m.A1 = m.A0;
+  m.C1 = m.C0;
+  PhiArgs a;
+  a.bias = nullptr;
+  a.scale = 1.f;
+  a.temp0 = nullptr;
+  a.temp1 = nullptr;
+  a.rows = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.heads = 1;
+  a.nsets = 1;
+  a.m = (int)N;
+  a.ident_from = 0;
+  a.tcol0 = 0;
+  a.tcol1 = 0;
+  a.status = status;
+  if (a_mn && b_mn) return launch_act<FAKLA_ACT_IDENTITY, true, true>(m, a, M, N, tiling, stream);
+  if (a_mn) return launch_act<FAKLA_ACT_IDENTITY, true, false>(m, a, M, N, tiling, stream);
+  if (b_mn) return launch_act<FAKLA_ACT_IDENTITY, false, true>(m, a, M, N, tiling, stream);
+  return launch_act<FAKLA_ACT_IDENTITY, false, false>(m, a, M, N, tiling, stream);
 }
 
 bool qkv_sm100_supported(int64_t rows, int64_t K, int64_t feat, int64_t vdim, int64_t heads) {

@@ -104,6 +104,13 @@ def test_argument_validation_without_device():
     assert rc == 1 and b"non-NULL" in lib.fakla_last_error()
     rc = lib.fakla_decode_noalloc(p, p, p, None, p, None, p, p, p, N, H * 512, H, 512, M, 1, None)
     assert rc == 2 and b"head dims" in lib.fakla_last_error()
+    # linear-layer gradients: dpre is required, dx needs W, db needs a workspace
+    rc = lib.fakla_linear_backward(p, p, None, p, None, None, 8, 8, 8, 1, None, 0, None)
+    assert rc == 1
+    rc = lib.fakla_linear_backward(p, None, p, p, None, None, 8, 8, 8, 1, None, 0, None)
+    assert rc == 1
+    rc = lib.fakla_linear_backward(p, p, p, None, None, p, 8, 8, 8, 1, None, 0, None)
+    assert rc == 6
 
 
 def test_workspace_queries():
