@@ -66,6 +66,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kOutWarpBytes = 32 * 128;              // 32 rows x 64 bf16
 constexpr int kOutBytes = kEpiWarps * kOutWarpBytes;  // 32 KB (one buffer per warp)
 constexpr int kThreads = 64 + 32 * kEpiWarps;        // 320
+constexpr uint32_t kEpiBarrier = 1;                  // named barrier of the epilogue warps
 template <int BNT> constexpr uint32_t kTmemColsT = 2 * BNT;  // 512 (BNT = 256)
 constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
 
@@ -84,6 +85,14 @@ __device__ __forceinline__ float reduce_2pi(float x) {
   constexpr float k2PiLo = -1.7484556025237907e-07f;  // 2 pi - float(2 pi)
   const float k = rintf(x * kInv2Pi);
   return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+}
+
+// 2^x by the MUFU's approximation (relative error far below the bf16
+// rounding applied to the output); as raw bits.
+__device__ __forceinline__ uint32_t ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return __float_as_uint(r);
 }
 
 struct PhiArgs {
@@ -352,7 +361,27 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     int acc = 0;
     uint32_t acc_phase = 0;
     bool stored = false;
-    for (int u = tile0; u < total_units && !*abort_flag; u += tile_step) {
+    for (int u = tile0; u < total_units; u += tile_step) {
+      // One epilogue warp polls the accumulator barrier (and the abort flag);
+      // the other seven sleep in a named barrier, which takes no issue slots.
+      // Eight polling warps spent most of the kernel's instructions, and under
+      // the power cap that cost clock. The barrier also hands every warp the
+      // same stop decision, so none leaves the loop while others wait in it.
+      bool stop = false;
+      if (ew == 0) {
+        stop = *abort_flag != 0;
+        if (!stop) {
+          // Pair: rank 0's commit lands on both CTAs' `tfull`.
+          const bool ready = rank == 0 ? mbar_wait(&tfull[acc], acc_phase, kWaitNs)
+                                       : mbar_wait_cluster(&tfull[acc], acc_phase, kWaitNs);
+          if (!ready) {
+            if (lane == 0) report_status(args.status, FAKLA_ERR_TIMEOUT);
+            *abort_flag = 1;
+            stop = true;
+          }
+        }
+      }
+      if (named_barrier_or(kEpiBarrier, 32 * kEpiWarps, stop)) break;
       const Unit t = unit_at(u);
       // columns of this warp: half of the unit's (BNT or BNT / 2)
       const int wcols = t.whole ? kWarpCols : kWarpCols / 2;
@@ -361,14 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       const CUtensorMap* mapC = t.set == 0 ? &tmC0 : &tmC1;
       const __nv_bfloat16* temp = t.set == 0 ? args.temp0 : args.temp1;
       const int grow = row0 + 32 * q + lane;  // this thread's output row
-      // Pair: rank 0's commit lands on both CTAs' `tfull`.
-      const bool ready = rank == 0 ? mbar_wait(&tfull[acc], acc_phase, kWaitNs)
-                                   : mbar_wait_cluster(&tfull[acc], acc_phase, kWaitNs);
-      if (!ready) {
-        report_status(args.status, FAKLA_ERR_TIMEOUT);
-        *abort_flag = 1;
-        break;
-      }
       tc_fence_after();
       const uint32_t t_row =
           tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BNT + half * wcols);
@@ -439,10 +460,19 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             } else {
               uint64_t y;
               if constexpr (ACT == FAKLA_ACT_ELU1) {
-                // elu(x) + 1 = x + 1 (x > 0) or exp(x), the pair's x + 1 in one op
+                // elu(x) + 1 = x + 1 for x > 0, e^x = 2^(x log2 e) otherwise: the
+                // pair's x + 1 and x log2 e one paired op each, the two powers of
+                // two on the MUFU (ex2.approx; the result is rounded to bf16), and
+                // the choice by the sign bit in one bitwise select each (x = -0
+                // takes 2^-0 = 1 = 0 + 1). The epilogue shares issue slots with the
+                // producer and MMA threads, so its instruction count shows in the
+                // tensor pipe's activity.
                 const float2 p1 = f2_split(f2_add(x, f2_splat(1.f)));
-                y = f2_make(__float_as_uint(a > 0.f ? p1.x : __expf(a)),
-                            __float_as_uint(b > 0.f ? p1.y : __expf(b)));
+                const float2 t = f2_split(f2_mul(x, f2_splat(1.4426950408889634f)));
+                const uint32_t ma = (uint32_t)((int32_t)__float_as_uint(a) >> 31);
+                const uint32_t mb = (uint32_t)((int32_t)__float_as_uint(b) >> 31);
+                y = f2_make((ex2_approx(t.x) & ma) | (__float_as_uint(p1.x) & ~ma),
+                            (ex2_approx(t.y) & mb) | (__float_as_uint(p1.y) & ~mb));
               } else {
                 y = f2_make(__float_as_uint(activate<ACT, true>(a)), __float_as_uint(activate<ACT, true>(b)));
               }

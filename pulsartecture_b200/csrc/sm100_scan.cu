@@ -838,32 +838,42 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         srow_len = hd;
         if (!kRaw) z0 = args.z[bh * hd + r];
       }
+      // 32 values per round trip to global memory (the loads of a piece are
+      // all issued before any is used): this load sits on the first chunk's
+      // path to MMA2, which short segments feel
 #pragma unroll 1
-      for (int cc = 0; cc < D; cc += 16) {
-        uint32_t v[16];
-        float f[16];
-        if (srow != nullptr && cc < srow_len) {
-          const float4* s4 = reinterpret_cast<const float4*>(srow + cc);
+      for (int c32 = 0; c32 < D; c32 += 32) {
+        float f[32];
+        if (srow != nullptr && c32 < srow_len) {
+          // srow_len is 128 or 64, so a 32-wide piece is whole
+          const float4* s4 = reinterpret_cast<const float4*>(srow + c32);
+          float4 x[8];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float4 x = s4[g];
-            f[4 * g] = x.x;
-            f[4 * g + 1] = x.y;
-            f[4 * g + 2] = x.z;
-            f[4 * g + 3] = x.w;
+          for (int g = 0; g < 8; ++g) x[g] = s4[g];
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            f[4 * g] = x[g].x;
+            f[4 * g + 1] = x[g].y;
+            f[4 * g + 2] = x[g].z;
+            f[4 * g + 3] = x[g].w;
           }
         } else if (scol != nullptr) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) f[e] = cc + e < srow_len ? scol[(int64_t)(cc + e) * srow_len] : 0.f;
+          for (int e = 0; e < 32; ++e) f[e] = c32 + e < srow_len ? scol[(int64_t)(c32 + e) * srow_len] : 0.f;
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) f[e] = 0.f;
+          for (int e = 0; e < 32; ++e) f[e] = 0.f;
         }
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(f[e]);
-        tmem_st16(lane_addr + kColS + (uint32_t)cc, v);
-        put_sb8<kRaw>(sSb, sSbLo, r, cc, f);
-        put_sb8<kRaw>(sSb, sSbLo, r, cc + 8, f + 8);
+        for (int h16 = 0; h16 < 32; h16 += 16) {
+          const int cc = c32 + h16;
+          uint32_t v[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(f[h16 + e]);
+          tmem_st16(lane_addr + kColS + (uint32_t)cc, v);
+          put_sb8<kRaw>(sSb, sSbLo, r, cc, f + h16);
+          put_sb8<kRaw>(sSb, sSbLo, r, cc + 8, f + h16 + 8);
+        }
       }
       if constexpr (kZ) {
         tmem_st1(lane_addr + kColZ, __float_as_uint(z0));
