@@ -58,7 +58,7 @@ UNIT = "tokens/s"
 # DRAM bytes (read + write) per launch of each kernel at the 1-GPU shapes
 # (B=8, H=16, T=4096), from one ncu capture each (dram__bytes_read.sum +
 # dram__bytes_write.sum).
-PROFILED_DRAM_BYTES = {"phi_gemm_sm100": 276.9e6 + 234.2e6, "scan_sm100": 402.7e6 + 112.2e6}
+PROFILED_DRAM_BYTES = {"phi_gemm_sm100": 276.9e6 + 234.8e6, "scan_sm100": 402.7e6 + 112.8e6}
 
 
 def peaks():
@@ -287,6 +287,31 @@ def workload_config(world, partition):
 
 
 # ----------------------------------------------------------------------------- single kernel
+def run_prefill_only(args):
+    """The headline prefill step alone (fakla_prefill: phi GEMM, then the scan),
+    for launch lists: the whole B=8, H=16, T=4096 problem, or with --shard-of N
+    rank 0's part of an N-way split (--partition batch or head). Prints the mean
+    device time per step."""
+    from pulsartecture_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    W, bias = lpm_init(IN_DIM, H * D)
+    W, bias = W.bfloat16().to(dev), bias.bfloat16().to(dev)
+    part = "batch" if args.partition == "auto" else args.partition
+    shard = PrefillShard(L, dev, part, args.shard_of, 0, B, T, H, W, bias, 1000)
+    for _ in range(args.warmup):
+        shard.step()
+    torch.cuda.synchronize()
+    ms = time_loop(shard.step, args.steps, torch.cuda.current_stream(dev)) / args.steps
+    _lib.check(L.fakla_device_status(shard.sh))
+    print(json.dumps({"only": "prefill", "shard_of": args.shard_of, "partition": part, "batch": shard.B,
+                      "heads": shard.H, "launches_per_step": shard.launches_per_step(), "ms_per_step": ms}),
+          flush=True)
+    return 0
+
+
 def run_only(args):
     """One kernel of the path alone, on the benchmark's shapes: `phi` = the
     phi GEMM for q and k of the B=8, H=16, T=4096 prefill (2*65536 rows), `scan` =
@@ -959,7 +984,10 @@ def main():
     ap.add_argument("--no-longctx", action="store_true")
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
-    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx", "mixer"],
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="with --only prefill: time rank 0's part of an N-way split on one GPU")
+    ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx", "mixer",
+                                       "prefill"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -973,6 +1001,8 @@ def main():
         return run_longctx(args)
     if args.only == "mixer":
         return run_mixer(args)
+    if args.only == "prefill":
+        return run_prefill_only(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
