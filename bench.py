@@ -312,6 +312,28 @@ def run_prefill_only(args):
     return 0
 
 
+def run_decode_step_only(args):
+    """The whole decode step (fakla_decode: the map GEMM for q and k, then the
+    state kernel) of batch 256, H=32, or with --shard-of N rank 0's 256/N
+    sequences of an N-way batch split. Prints the mean device time per step."""
+    from pulsartecture_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    Wd, bd = lpm_init(DEC_IN, DEC_H * D)
+    Wd, bd = Wd.bfloat16().to(dev), bd.bfloat16().to(dev)
+    sh = DecodeShard(L, dev, args.shard_of, 0, Wd, bd)
+    for _ in range(args.warmup):
+        sh.step()
+    torch.cuda.synchronize()
+    ms = time_loop(sh.step, args.steps, torch.cuda.current_stream(dev)) / args.steps
+    _lib.check(L.fakla_device_status(sh.sh))
+    print(json.dumps({"only": "decode_step", "shard_of": args.shard_of, "sequences": sh.N, "ms_per_step": ms,
+                      "tokens_per_s_if_all_ranks": DEC_N / (ms * 1e-3)}), flush=True)
+    return 0
+
+
 def run_only(args):
     """One kernel of the path alone, on the benchmark's shapes: `phi` = the
     phi GEMM for q and k of the B=8, H=16, T=4096 prefill (2*65536 rows), `scan` =
@@ -985,9 +1007,9 @@ def main():
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--shard-of", type=int, default=1,
-                    help="with --only prefill: time rank 0's part of an N-way split on one GPU")
+                    help="with --only prefill or decode_step: time rank 0's part of an N-way split on one GPU")
     ap.add_argument("--only", choices=["phi", "scan", "decode", "backward", "sustained", "lm", "longctx", "mixer",
-                                       "prefill"],
+                                       "prefill", "decode_step"],
                     help="launch just one kernel (warmup + steps launches) for profiler captures; "
                          "'sustained' runs each kernel for ~1.5 s and reports clocks and power")
     args = ap.parse_args()
@@ -1003,6 +1025,8 @@ def main():
         return run_mixer(args)
     if args.only == "prefill":
         return run_prefill_only(args)
+    if args.only == "decode_step":
+        return run_decode_step_only(args)
     if args.only:
         return run_only(args)
     assert args.warmup >= 3, "at least 3 warm-up steps"
