@@ -480,7 +480,7 @@ def run_sustained(args):
 # ----------------------------------------------------------------------------- long context
 def run_longctx(args):
     """Long-context prefill on one GPU: B=1, H=32, T=65536, Dk=Dv=M=128, bf16,
-    LearnablePositiveMap(4096 -> 4096) fused (fa_kla). The 32 sequences would
+    LearnablePositiveMap(4096 -> 4096) (fa_kla: one call, two launches). The 32 sequences would
     leave most SMs idle, so the scan runs segmented (segment sums, a prefix,
     then one CTA per segment). Prints tokens/s, the phi GEMM and scan times
     and the whole prefill's rate against the measured tensor peak."""
@@ -524,7 +524,7 @@ def run_longctx(args):
     _lib.check(L.fakla_device_status(sh))
     _, tflops_burst, _, _ = peaks()
     flops = 2 * (2 * T_) * (H_ * D_) * (H_ * D_) + T_ * H_ * 98304
-    line = {"only": "longctx", "workload": "FA-KLA prefill B=1, H=32, T=65536, Dk=Dv=M=128, bf16, phi 4096->4096 fused",
+    line = {"only": "longctx", "workload": "FA-KLA prefill B=1, H=32, T=65536, Dk=Dv=M=128, bf16, phi 4096->4096",
             "ms": round(res["prefill"], 4), "tokens_per_s": round(T_ / res["prefill"] * 1e3, 1),
             "phi_ms": round(res["phi"], 4), "scan_ms": round(res["prefill"] - res["phi"], 4),
             "tflops": round(flops / res["prefill"] / 1e9, 1),
@@ -1222,7 +1222,7 @@ def main():
 
     # ---- module forward (TMLinKernelAttn, embed 2048 -> 16 heads of 128, bf16, inference) at 1 GPU:
     # projections folded into the feature map (one GEMM + scan) against the
-    # projections as three library GEMMs followed by the fused prefill
+    # projections as three library GEMMs followed by fakla_prefill
     module = None
     if not args.no_module and world == 1:
         from pulsartecture_b200.attention import TMLinKernelAttn

@@ -49,8 +49,8 @@ class LinearProjection(nn.Module):
             if self.use_bias and self.linear.bias is not None:
                 nn.init.zeros_(self.linear.bias)
         else:
-            raise ValueError(f"Unsupported initialization scheme: {scheme}. "
-                             "Choose 'xavier_uniform', 'kaiming_uniform', or False.")
+            raise ValueError(f"initialize={scheme!r} is not a known scheme (use 'kaiming_uniform', "
+                             "'xavier_uniform', True or False)")
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.dtype != self.linear.weight.dtype:
@@ -63,9 +63,9 @@ class LinearProjection(nn.Module):
         return x
 
     def extra_repr(self) -> str:
-        s = f"in_dim={self.in_dim}, out_dim={self.out_dim}, bias={self.use_bias}"
+        parts = [f"{self.in_dim} -> {self.out_dim}", f"bias={self.use_bias}"]
         if self.norm is not None:
-            s += f", norm=True (eps={self.norm.eps}, affine={self.norm.elementwise_affine})"
+            parts.append(f"layernorm(eps={self.norm.eps}, affine={self.norm.elementwise_affine})")
         if self.activation is not None:
-            s += f", activation={self.activation.__class__.__name__}"
-        return s
+            parts.append(type(self.activation).__name__)
+        return ", ".join(parts)
