@@ -69,6 +69,10 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;        // 320
 constexpr uint32_t kEpiBarrier = 1;                  // named barrier of the epilogue warps
 template <int BNT> constexpr uint32_t kTmemColsT = 2 * BNT;  // 512 (BNT = 256)
 constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
+// Suspend-time hint of the pipeline's barrier polls: a waiting thread sleeps
+// until the phase completes (or this long) instead of spinning, so the
+// producer, the MMA issuer and the epilogue's poller spend few issue slots.
+constexpr uint32_t kSleepNs = 50000;
 
 template <int BNT, bool PAIR>
 constexpr size_t kSmemBytesT = 1024 /*align slack*/ +
@@ -232,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         const CUtensorMap* mapB = t.whole ? &tmB : &tmBh;
         const uint32_t stage_tx = (uint32_t)(kABytes + brows * BK * 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const bool free = rank == 0 ? mbar_wait(&empty[stage], phase ^ 1u, kWaitNs)
-                                      : mbar_wait_cluster(&empty[stage], phase ^ 1u, kWaitNs);
+          const bool free = rank == 0 ? mbar_wait_hint(&empty[stage], phase ^ 1u, kWaitNs, kSleepNs)
+                                      : mbar_wait_cluster_hint(&empty[stage], phase ^ 1u, kWaitNs, kSleepNs);
           if (!free) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
@@ -297,8 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       uint32_t acc_phase = 0;
       for (int u = tile0; u < total_units && !*abort_flag; u += tile_step) {
         const uint32_t idesc = u < n_full ? idesc_whole : idesc_half;
-        const bool drained = PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, kWaitNs)
-                                  : mbar_wait(&tempty[acc], acc_phase ^ 1u, kWaitNs);
+        const bool drained = PAIR ? mbar_wait_cluster_hint(&tempty[acc], acc_phase ^ 1u, kWaitNs, kSleepNs)
+                                  : mbar_wait_hint(&tempty[acc], acc_phase ^ 1u, kWaitNs, kSleepNs);
         if (!drained) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BNT);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, kWaitNs)) {
+          if (!mbar_wait_hint(&full[stage], phase, kWaitNs, kSleepNs)) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
@@ -372,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         stop = *abort_flag != 0;
         if (!stop) {
           // Pair: rank 0's commit lands on both CTAs' `tfull`.
-          const bool ready = rank == 0 ? mbar_wait(&tfull[acc], acc_phase, kWaitNs)
-                                       : mbar_wait_cluster(&tfull[acc], acc_phase, kWaitNs);
+          const bool ready = rank == 0 ? mbar_wait_hint(&tfull[acc], acc_phase, kWaitNs, kSleepNs)
+                                       : mbar_wait_cluster_hint(&tfull[acc], acc_phase, kWaitNs, kSleepNs);
           if (!ready) {
             if (lane == 0) report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;

@@ -81,6 +81,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   return true;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep until the phase
+// completes or `hint_ns` pass, instead of coming back at once; waits that
+// last long (a producer waiting for a free stage, the epilogue waiting for a
+// whole tile) then spend far fewer issue slots polling.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (as mbar_wait) that sleeps up to hint_ns per poll.
+__device__ __forceinline__ bool mbar_wait_hint(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                               uint32_t hint_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_hint(bar, parity, hint_ns)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
 // ----------------------------------------------------------------- cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -113,6 +140,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait (as mbar_wait) with cluster-scope acquire, for barriers that
 // the other CTA of a pair arrives on.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
@@ -122,6 +161,17 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   uint32_t n = 0;
   while (!mbar_try_wait_cluster(bar, parity)) {
     if ((++n & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+// Cluster-scope bounded wait that sleeps up to hint_ns per poll.
+__device__ __forceinline__ bool mbar_wait_cluster_hint(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                       uint32_t hint_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster_hint(bar, parity, hint_ns)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
   return true;
 }
