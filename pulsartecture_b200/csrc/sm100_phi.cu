@@ -109,6 +109,8 @@ struct PhiArgs {
   int ident_from;              // columns >= ident_from skip the activation (N: none)
   int tcol0, tcol1;            // temperature applies to columns [tcol0, tcol1)
   int n_full;                  // tiles [0, n_full) run whole, the rest as two column halves
+  int a_rows;                  // rows of x per A box (BM, or fewer when a row set has fewer
+                               // than BM rows: the rest of each A stage stays zero)
   int* status;
 };
 
@@ -206,6 +208,20 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
       tmem_relinquish();
     }
   }
+  // A row set of fewer than BM rows (a decode step of few sequences) loads only
+  // its rows: the TMA would otherwise move the zero fill of a whole BM-row box
+  // through the crossbar on every stage. The rows past a_rows are zeroed once
+  // here and never written again, so the MMAs read zeros there.
+  if constexpr (!PAIR && !AMN) {
+    if (args.a_rows < BM) {
+      const int from = args.a_rows * 128 / 16, to = BM * 128 / 16;  // uint4 offsets within a stage
+      for (int s = 0; s < kStages; ++s) {
+        uint4* dst = reinterpret_cast<uint4*>(sA + s * kABytes);
+        for (int o = from + (int)threadIdx.x; o < to; o += kThreads) dst[o] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   // a pair's barriers must be initialised before the other CTA signals them
@@ -234,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
         const int col0 = (t.r % col_tiles) * BNT + t.coff + (int)rank * brows;
         const CUtensorMap* mapA = t.set == 0 ? &tmA0 : &tmA1;
         const CUtensorMap* mapB = t.whole ? &tmB : &tmBh;
-        const uint32_t stage_tx = (uint32_t)(kABytes + brows * BK * 2);
+        const uint32_t stage_tx = (uint32_t)((AMN ? BM : args.a_rows) * BK * 2 + brows * BK * 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const bool free = rank == 0 ? mbar_wait_hint(&empty[stage], phase ^ 1u, kWaitNs, kSleepNs)
                                       : mbar_wait_cluster_hint(&empty[stage], phase ^ 1u, kWaitNs, kSleepNs);
@@ -600,6 +616,11 @@ static int pick_tiling(int64_t rows, int64_t N, int nsets) {
 static int tiling_bn(int tiling) { return tiling == kTile128 ? 128 : BN; }
 // rows of W per CTA per stage (the TMA box height of the W map)
 static int tiling_b_rows(int tiling) { return tiling == kTilePair ? BN / 2 : tiling_bn(tiling); }
+// rows of x per A box: a single-CTA launch whose row sets have fewer than BM
+// rows loads only those (rounded up to 8), not a whole BM-row box
+static int a_box_rows(int64_t rows, int tiling) {
+  return (tiling != kTilePair && rows < BM) ? (int)((rows + 7) / 8 * 8) : BM;
+}
 
 // Tensor maps of one launch: x rows of both row sets, W (box of a CTA's rows
 // of a whole tile, and of half a tile for the split tail), outputs.
@@ -672,10 +693,11 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   const int nsets = x1 != nullptr ? 2 : 1;
   const int tiling = pick_tiling(rows, N, nsets);
   const uint64_t out_cols = (uint64_t)N * (act == FAKLA_ACT_COSSIN ? 2 : 1);
-  bool ok = make_map_2d(&m.A0, x0, (uint64_t)K, (uint64_t)rows, BK, BM) && make_w_maps(&m, W, K, N, tiling) &&
-            make_map_2d(&m.C0, out0, out_cols, (uint64_t)rows, 64, 32);
+  const int a_rows = a_box_rows(rows, tiling);
+  bool ok = make_map_2d(&m.A0, x0, (uint64_t)K, (uint64_t)rows, BK, (uint32_t)a_rows) &&
+            make_w_maps(&m, W, K, N, tiling) && make_map_2d(&m.C0, out0, out_cols, (uint64_t)rows, 64, 32);
   if (ok && nsets == 2)
-    ok = make_map_2d(&m.A1, x1, (uint64_t)K, (uint64_t)rows, BK, BM) &&
+    ok = make_map_2d(&m.A1, x1, (uint64_t)K, (uint64_t)rows, BK, (uint32_t)a_rows) &&
          make_map_2d(&m.C1, out1, out_cols, (uint64_t)rows, 64, 32);
   else {
     m.A1 = m.A0;
@@ -697,6 +719,7 @@ cudaError_t launch_phi_sm100(const void* x0, const void* x1, const void* W, cons
   a.ident_from = (int)N;
   a.tcol0 = 0;
   a.tcol1 = (int)N;
+  a.a_rows = a_rows;
   a.status = status;
   switch (act) {
     case FAKLA_ACT_ELU1: return launch_act<FAKLA_ACT_ELU1>(m, a, rows, N, tiling, stream);
@@ -735,8 +758,9 @@ cudaError_t launch_gemm_sm100(const void* A, bool a_mn, const void* B, bool b_mn
   PhiMaps m;
   const int tiling = pick_tiling(M, N, 1);
   const uint32_t brows = (uint32_t)tiling_b_rows(tiling);
+  const int a_rows = a_mn ? BM : a_box_rows(M, tiling);
   bool ok = a_mn ? make_map_2d(&m.A0, A, (uint64_t)M, (uint64_t)K, 64, BK)
-                 : make_map_2d(&m.A0, A, (uint64_t)K, (uint64_t)M, BK, BM);
+                 : make_map_2d(&m.A0, A, (uint64_t)K, (uint64_t)M, BK, (uint32_t)a_rows);
   if (b_mn)
     ok = ok && make_map_2d(&m.B, B, (uint64_t)N, (uint64_t)K, 64, BK) &&
          make_map_2d(&m.Bh, B, (uint64_t)N, (uint64_t)K, 64, BK);
@@ -762,6 +786,7 @@ cudaError_t launch_gemm_sm100(const void* A, bool a_mn, const void* B, bool b_mn
   a.ident_from = 0;
   a.tcol0 = 0;
   a.tcol1 = 0;
+  a.a_rows = a_rows;
   a.status = status;
   if (a_mn && b_mn) return launch_act<FAKLA_ACT_IDENTITY, true, true>(m, a, M, N, tiling, stream);
   if (a_mn) return launch_act<FAKLA_ACT_IDENTITY, true, false>(m, a, M, N, tiling, stream);
@@ -782,8 +807,9 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
   const int64_t N = 2 * feat + vdim;
   const int tiling = pick_tiling(rows, N, 1);
   PhiMaps m;
-  const bool ok = make_map_2d(&m.A0, x, (uint64_t)K, (uint64_t)rows, BK, BM) && make_w_maps(&m, W, K, N, tiling) &&
-                  make_map_2d(&m.C0, out, (uint64_t)N, (uint64_t)rows, 64, 32);
+  const int a_rows = a_box_rows(rows, tiling);
+  const bool ok = make_map_2d(&m.A0, x, (uint64_t)K, (uint64_t)rows, BK, (uint32_t)a_rows) &&
+                  make_w_maps(&m, W, K, N, tiling) && make_map_2d(&m.C0, out, (uint64_t)N, (uint64_t)rows, 64, 32);
   m.A1 = m.A0;
   m.C1 = m.C0;
   *encoded = ok;
@@ -802,6 +828,7 @@ cudaError_t launch_qkv_sm100(const void* x, const void* W, const void* bias, con
   a.ident_from = (int)(2 * feat);  // [phi(q) | phi(k) * temp | v]
   a.tcol0 = (int)feat;
   a.tcol1 = (int)(2 * feat);
+  a.a_rows = a_rows;
   a.status = status;
   return launch_act<FAKLA_ACT_ELU1>(m, a, rows, N, tiling, stream);
 }
