@@ -79,3 +79,37 @@ def test_two_gloo_ranks_reproduce_single_process():
         np.testing.assert_array_equal(got["out"], ref_out)
         np.testing.assert_array_equal(got["S"], ref_S)
         np.testing.assert_array_equal(got["outb"], ref_out)
+
+
+def _gather_worker(rank, world, port, outdir):
+    """The bench's gather of shards (its NCCL path on CUDA tensors; gloo here)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import bench
+
+    full = torch.arange(4 * 6 * 8, dtype=torch.float32).reshape(4, 6, 8)
+    b0, b1 = shard_range(4, world, rank)
+    h0, h1 = shard_range(6, world, rank)
+    by_batch = bench.gather_cat(full[b0:b1], world, 0)
+    by_head = bench.gather_cat(full[:, h0:h1], world, 1)
+    if rank == 0:
+        same = bench.compare(by_batch, full)
+        off = bench.compare(by_head + 1e-3, full)
+        np.savez(os.path.join(outdir, "g.npz"), b=by_batch.numpy(), h=by_head.numpy(),
+                 same=np.array([same["bit_exact"], same["max_abs"], same["rel_l2"]]),
+                 off=np.array([off["bit_exact"], off["max_abs"]]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_bench_gather_of_batch_and_head_shards():
+    full = np.arange(4 * 6 * 8, dtype=np.float32).reshape(4, 6, 8)
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_gather_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
+        with np.load(os.path.join(d, "g.npz")) as z:
+            got = {k: z[k] for k in z.files}
+    np.testing.assert_array_equal(got["b"], full)
+    np.testing.assert_array_equal(got["h"], full)
+    assert got["same"][0] == 1 and got["same"][1] == 0 and got["same"][2] == 0
+    assert got["off"][0] == 0 and abs(got["off"][1] - 1e-3) < 1e-4  # fp32 rounding of x + 1e-3
