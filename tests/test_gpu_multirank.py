@@ -9,9 +9,10 @@ each takes its own. Head shards take the matching rows of the feature map and
 whole q, k rows (the map mixes all heads of a row), which is the split a
 multi-GPU run uses when it divides heads.
 
-T=1024 with 4 sequences per rank makes each rank's scan run segmented
-(segment sums, prefix, one CTA per segment), as the small per-GPU problems of
-an 8-GPU split do.
+T=1000 (a ragged last chunk) with 4 sequences per rank makes each rank's scan
+run segmented (segment sums, prefix, one CTA per segment), as the small
+per-GPU problems of an 8-GPU split do; a per-(token, head) temperature rides
+along, split with its heads or batch rows.
 """
 import math
 import os
@@ -28,7 +29,7 @@ from tests.helpers import BF16_MAX_ABS, BF16_REL_L2, lpm_params, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-B, T, H, D = 2, 1024, 4, 128
+B, T, H, D = 2, 1000, 4, 128
 
 
 def _free_port():
@@ -43,24 +44,25 @@ def _inputs():
     k = (torch.randn(B, T, H * D, generator=g) / math.sqrt(D)).bfloat16()
     v = (torch.randn(B, T, H, D, generator=g) / math.sqrt(D)).bfloat16()
     W, b = lpm_params(H * D, H * D, seed=22, dtype=torch.bfloat16)
-    return q, k, v, W, b
+    tp = (torch.rand(B, T, H, generator=g) + 0.5).bfloat16()
+    return q, k, v, W, b, tp
 
 
-def _prefill(dev, q, k, v, W, b):
+def _prefill(dev, q, k, v, W, b, tp):
     """fakla_prefill through the C ABI; returns (out, S, z) on the host."""
     from pulsartecture_b200 import _lib
 
     L = _lib.lib()
     Bl, Tl, Hl = v.shape[0], v.shape[1], v.shape[2]
     in_dim = q.shape[-1]
-    q, k, v, W, b = (t.to(dev).contiguous() for t in (q, k, v, W, b))
+    q, k, v, W, b, tp = (t.to(dev).contiguous() for t in (q, k, v, W, b, tp))
     out = torch.empty(Bl, Tl, Hl, D, device=dev, dtype=torch.bfloat16)
     S = torch.empty(Bl, Hl, D, D, device=dev)
     z = torch.empty(Bl, Hl, D, device=dev)
     ws_bytes = L.fakla_prefill_workspace_bytes(Bl, Tl, in_dim, Hl, D, D, _lib.FAKLA_BF16)
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    _lib.check(L.fakla_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), None, W.data_ptr(), b.data_ptr(),
+    _lib.check(L.fakla_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), tp.data_ptr(), W.data_ptr(), b.data_ptr(),
                                out.data_ptr(), S.data_ptr(), z.data_ptr(), Bl, Tl, in_dim, Hl, D, D,
                                _lib.FAKLA_BF16, _lib.FAKLA_STATE_OUT, ws.data_ptr(), ws_bytes, stream))
     _lib.check(L.fakla_device_status(stream))
@@ -76,15 +78,15 @@ def _worker(rank, world, port, outdir):
 
     dev = torch.device("cuda", rank % torch.cuda.device_count())
     torch.cuda.set_device(dev)
-    q, k, v, W, b = _inputs()
+    q, k, v, W, b, tp = _inputs()
     # head shard: every batch row, heads [h0, h1), the matching map rows
     h0, h1, w_r, b_r = head_shard(W, b, H, world, rank)
-    oh, Sh, zh, seg_h = _prefill(dev, q, k, v[:, :, h0:h1], w_r, b_r)
+    oh, Sh, zh, seg_h = _prefill(dev, q, k, v[:, :, h0:h1], w_r, b_r, tp[:, :, h0:h1])
     hparts = [None] * world
     dist.all_gather_object(hparts, (h0, oh, Sh, zh, seg_h))
     # batch shard: rows [r0, r1), every head
     r0, r1 = batch_shard(B, world, rank)
-    ob, Sb, zb, seg_b = _prefill(dev, q[r0:r1], k[r0:r1], v[r0:r1], W, b)
+    ob, Sb, zb, seg_b = _prefill(dev, q[r0:r1], k[r0:r1], v[r0:r1], W, b, tp[r0:r1])
     bparts = [None] * world
     dist.all_gather_object(bparts, (r0, ob, Sb, zb, seg_b))
     if rank == 0:
@@ -105,10 +107,10 @@ def _worker(rank, world, port, outdir):
 def test_two_ranks_head_and_batch_shards_on_the_kernels(cuda):
     from oracle import fakla_oracle as O
 
-    q, k, v, W, b = _inputs()
+    q, k, v, W, b, tp = _inputs()
     f = lambda t: t.float().numpy()  # noqa: E731
-    eo, eS, ez = O.prefill(f(q), f(k), f(v), f(W), f(b))
-    whole_out, whole_S, whole_z, _ = _prefill(cuda, q, k, v, W, b)
+    eo, eS, ez = O.prefill(f(q), f(k), f(v), f(W), f(b), f(tp))
+    whole_out, whole_S, whole_z, _ = _prefill(cuda, q, k, v, W, b, tp)
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_worker, args=(2, _free_port(), d), nprocs=2, join=True, start_method="spawn")
         with np.load(os.path.join(d, "gathered.npz")) as npz:
