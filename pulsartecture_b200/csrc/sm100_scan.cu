@@ -70,6 +70,10 @@ constexpr uint32_t kTmemCols = 512;
 // and the two parity slots of the per-row sum of the masked P.
 constexpr uint32_t kColP = 0, kColO = 128, kColS = 256, kColZ = 384, kColDz = 400, kColRs = 416;
 constexpr uint64_t kWaitNs = 2000000000ull;
+// Longest sleep per poll of a barrier wait (the thread wakes when the phase
+// completes): waiting warps then take fewer issue slots from the working
+// warps of their scheduler.
+constexpr uint32_t kSleepNs = 20000;
 constexpr int64_t kStateFloats = (int64_t)D * D + D;  // one (S, z) record
 
 // Shared memory. Barriers sit in the first 256 bytes of the dynamic window;
@@ -408,10 +412,15 @@ __device__ __forceinline__ float stage_affine_32(const uint32_t (&v)[32], float 
   return d.x + d.y;
 }
 
+// The bounded wait with a suspend-time hint.
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  return mbar_wait_hint(bar, parity, limit_ns, kSleepNs);
+}
+
 // Warp-uniform forms of the bounded wait and of the abort check, for warps
 // that go on to issue .sync.aligned tcgen05 loads and stores.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitNs));
+  return __all_sync(0xffffffffu, bar_wait(bar, parity, kWaitNs));
 }
 __device__ __forceinline__ bool warp_aborted(volatile int* abort_flag) {
   return __any_sync(0xffffffffu, *abort_flag != 0);
@@ -572,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if constexpr (kSplitV) {
           const int t0 = chunk_t0(i);
           // Q, K of chunk i: MMA1-MMA4 of chunk i-2 have read the stage
-          if (!mbar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
+          if (!bar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
@@ -586,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           ++issued;
           // V of chunk i: the stores of chunk i-2's output (staged in this
           // V tile) have read it
-          if (!mbar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
+          if (!bar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
@@ -597,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           ++issued_v;
           continue;
         }
-        if (!mbar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
+        if (!bar_wait(&bars[kEmpty0 + st], ph ^ 1u, kWaitNs)) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
           break;
@@ -609,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           for (int a = 0; a < na; ++a) tma_load_4d(sV + st * kTile + a * kAtom, &tmV, fb, a * 64, h, t0, b);
           ++issued;
           // one K tile: MMA4 of the previous chunk must have read it
-          if (i > 0 && !mbar_wait(&bars[kKFree], (uint32_t)(i - 1) & 1u, kWaitNs)) {
+          if (i > 0 && !bar_wait(&bars[kKFree], (uint32_t)(i - 1) & 1u, kWaitNs)) {
             report_status(args.status, FAKLA_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
@@ -624,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         }
         // The Q tile doubles as the output staging of chunk i-2: wait for
         // that store to have read it.
-        if (!mbar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
+        if (!bar_wait(&bars[kEmptyQ0 + st], ph ^ 1u, kWaitNs)) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
           break;
@@ -635,9 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
       if (*abort_flag) {
         // Let this CTA's own copies in flight land before the CTA exits.
         for (int i = issued - kStages; i < issued; ++i)
-          if (i >= 0) (void)mbar_wait(&bars[kFull0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
+          if (i >= 0) (void)bar_wait(&bars[kFull0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
         for (int i = issued_v - kStages; i < issued_v; ++i)
-          if (i >= 0) (void)mbar_wait(&bars[kFullV0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
+          if (i >= 0) (void)bar_wait(&bars[kFullV0 + (i & 1)], (uint32_t)(i >> 1) & 1u, kWaitNs);
       }
     }
   } else if (warp == 1) {
@@ -658,8 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         const int st = i & 1;
         const uint32_t ph = (uint32_t)(i >> 1) & 1u;
         const uint32_t par = (uint32_t)i & 1u, prev = (uint32_t)(i - 1) & 1u;
-        ok = mbar_wait(&bars[kFull0 + st], ph, kWaitNs);
-        if (ok && has_temp) ok = mbar_wait(&bars[kKReady], par, kWaitNs);
+        ok = bar_wait(&bars[kFull0 + st], ph, kWaitNs);
+        if (ok && has_temp) ok = bar_wait(&bars[kKReady], par, kWaitNs);
         if (!ok) break;
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + st * kTile);
@@ -671,8 +680,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
 #pragma unroll
         for (int j = 0; j < 8; ++j) mma_ss(tmem + kColP, kdesc(aQ, j), kdesc(aK, j), idP, j > 0);
         mma_commit(&bars[kBarP]);
-        ok = mbar_wait(&bars[kSReady], par, kWaitNs);
-        if (ok && i > 0) ok = mbar_wait(&bars[kOFree], prev, kWaitNs);
+        ok = bar_wait(&bars[kSReady], par, kWaitNs);
+        if (ok && i > 0) ok = bar_wait(&bars[kOFree], prev, kWaitNs);
         if (!ok) break;
         tc_fence_after();
         // MMA2 / MMA2b: O = Q S_{<c}, Dz = Q [z_hi z_lo]
@@ -687,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
           for (int j = 0; j < 8; ++j) mma_ss(tmem + kColDz, kdesc(aQ, j), zkdesc(aM0, j), idQZ, j > 0);
         }
         if constexpr (kSplitV) {
-          ok = mbar_wait(&bars[kFullV0 + st], ph, kWaitNs);
+          ok = bar_wait(&bars[kFullV0 + st], ph, kWaitNs);
           if (!ok) break;
           tc_fence_after();
         }
@@ -702,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if constexpr (kRaw) mma_commit(&bars[kKFree]);
         mma_commit(&bars[kBarS]);
         if constexpr (kSplitV) mma_commit(&bars[kEmptyQ0 + st]);  // Q, K of this stage read
-        ok = mbar_wait(&bars[kE1Done], par, kWaitNs);
+        ok = bar_wait(&bars[kE1Done], par, kWaitNs);
         if (!ok) break;
         tc_fence_after();
         // MMA3: O += Pm_hi V + Pm_lo V. Hi/lo of tokens [32g, 32g+32) sit in
@@ -734,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (issued_any) {
           // Drain the MMAs in flight before TMEM and smem are released.
           mma_commit(&bars[kDrain]);
-          (void)mbar_wait(&bars[kDrain], 0, kWaitNs);
+          (void)bar_wait(&bars[kDrain], 0, kWaitNs);
         }
       }
     }
@@ -1259,7 +1268,7 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
       for (int i = 0; i < nch && !*abort_flag; ++i) {
         const int st = i % kDStages;
         const uint32_t ph = (uint32_t)(i / kDStages) & 1u;
-        if (!mbar_wait(&bars[kDEmpty0 + st], ph ^ 1u, kWaitNs)) {
+        if (!bar_wait(&bars[kDEmpty0 + st], ph ^ 1u, kWaitNs)) {
           report_status(args.status, FAKLA_ERR_TIMEOUT);
           *abort_flag = 1;
           break;
@@ -1277,7 +1286,7 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
       if (*abort_flag) {
         for (int i = issued - kDStages; i < issued; ++i)
           if (i >= 0)
-            (void)mbar_wait(&bars[kDFull0 + i % kDStages], (uint32_t)(i / kDStages) & 1u, kWaitNs);
+            (void)bar_wait(&bars[kDFull0 + i % kDStages], (uint32_t)(i / kDStages) & 1u, kWaitNs);
       }
     }
   } else if (warp == 1) {
@@ -1290,8 +1299,8 @@ __global__ void __launch_bounds__(kDThreads, 1) scan_delta_sm100_kernel(
       for (int i = 0; i < nch && ok && !*abort_flag; ++i) {
         const int st = i % kDStages;
         const uint32_t ph = (uint32_t)(i / kDStages) & 1u;
-        ok = mbar_wait(&bars[kDFull0 + st], ph, kWaitNs);
-        if (ok && has_temp) ok = mbar_wait(&bars[kDKReady0 + st], ph, kWaitNs);
+        ok = bar_wait(&bars[kDFull0 + st], ph, kWaitNs);
+        if (ok && has_temp) ok = bar_wait(&bars[kDKReady0 + st], ph, kWaitNs);
         if (!ok) break;
         tc_fence_after();
         issued_any = true;
