@@ -273,7 +273,8 @@ int fakla_mix_features(const void* feats, const void* logits, void* out, int64_t
                        int64_t n_maps, int64_t feat_dim, int dtype, void* stream);
 
 /*
- * fakla_prefill -- feature map fused with FA-KLA: the hot path of
+ * fakla_prefill -- feature map and FA-KLA in one call (the phi GEMM, then
+ * the chunked scan as its programmatic dependent launch): the hot path of
  * TMLinKernelAttn.forward from the projected q/k/v onward (ultra_rwka/
  * attention/tm_kla.py:268-332: feature_mapper on q and k, head split,
  * temperature, fa_kla_attention).
@@ -340,7 +341,7 @@ int fakla_decode_mapped(const void* q_mapped, const void* k_mapped, const void* 
                         int64_t H, int64_t Df, int64_t Dv, int dtype, void* stream);
 
 /*
- * fakla_decode -- feature map fused with one recurrent step: phi(q), phi(k)
+ * fakla_decode -- feature map and one recurrent step in one call: phi(q), phi(k)
  * from projected rows q, k : (N, in_dim), then fakla_decode_mapped.
  * W : (H * M, in_dim), bias : (H * M) or NULL; v : (N, H, Dv);
  * temp : (N, H) or NULL; S : (N, H, M, Dv), z : (N, H, M) updated in place;

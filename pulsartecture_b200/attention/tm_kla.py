@@ -6,8 +6,8 @@ parameter names and initialisation, same checks and error types, same forward
 contract (x (B, T, embed_dim) -> (B, T, H*Dv)). The FA-KLA part of forward
 (feature map on q and k, temperature, causal kernelized attention,
 tm_kla.py:264-332) runs in libfakla: when the mapper is the default
-``LearnablePositiveMap`` (one linear layer + elu+1) phi is fused with the scan
-(``fakla_prefill``); any other ``FeatureMap`` is applied first and the mapped
+``LearnablePositiveMap`` (one linear layer + elu+1) phi and the scan run in one
+call (``fakla_prefill``: the phi GEMM, then the scan as its dependent launch); any other ``FeatureMap`` is applied first and the mapped
 tensors go through ``fakla_attention``.
 
 Extension (the reference is stateless): ``forward(..., state=None,
@@ -235,7 +235,7 @@ class TMLinKernelAttn(nn.Module):
         v = self.proj_v(x).reshape(N, H, Dv)
         mapper = self.feature_mapper
         if not (isinstance(mapper, LearnablePositiveMap) and mapper.fusable):
-            raise NotImplementedError("step() needs the fused LearnablePositiveMap (1 layer, elu+1)")
+            raise NotImplementedError("step() needs the one-call LearnablePositiveMap (1 layer, elu+1)")
         p = mapper.weight
         temp = None
         if self.temp_func is not None:
@@ -250,7 +250,7 @@ class TMLinKernelAttn(nn.Module):
 def fa_kla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[State] = None, *,
            phi_weight: torch.Tensor, phi_bias: Optional[torch.Tensor] = None,
            temp: Optional[torch.Tensor] = None, chunk: int = 128) -> Tuple[torch.Tensor, State]:
-    """Functional FA-KLA prefill with phi fused: ``forward(q, k, v, state) -> (out, state)``.
+    """Functional FA-KLA prefill with phi in the same call: ``forward(q, k, v, state) -> (out, state)``.
 
     q, k: (B, T, H_in, Dk) or (B, T, H_in*Dk) projected rows; v: (B, T, H, Dv);
     phi_weight: (H*M, H_in*Dk); phi_bias: (H*M,); temp: (B, T, H) or None.

@@ -202,7 +202,7 @@ def phi_map(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] 
 def fa_kla_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight: torch.Tensor,
                    bias: Optional[torch.Tensor] = None, temp: Optional[torch.Tensor] = None,
                    state: Optional[State] = None, return_state: bool = True):
-    """phi fused with FA-KLA (tm_kla.py:268-332 from the projected q/k/v on).
+    """phi and FA-KLA in one library call (tm_kla.py:268-332 from the projected q/k/v on).
 
     q, k: (B, T, in_dim) or (B, T, H_in, Dk) projected rows (phi mixes all heads
     of a row); v: (B, T, H, Dv); weight: (H*M, in_dim) -- the map rows of the H
@@ -343,14 +343,14 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
                         state: Optional[State] = None, return_state: bool = True,
                         out: Optional[torch.Tensor] = None, micro_batch: Optional[int] = None, slots: int = 3,
                         ordered: bool = True):
-    """phi fused with FA-KLA on HOST tensors, transfers overlapped with compute.
+    """phi and FA-KLA on HOST tensors, transfers overlapped with compute.
 
     q, k: (B, T, in_dim) or (B, T, H_in, Dk) on the CPU (pin them for
     asynchronous copies); v: (B, T, H, Dv) on the CPU; temp: (B, T, H) on the
     CPU or None; weight, bias and the optional input state on the GPU that
     runs the call. Sequences are independent, so the batch is cut into groups
     of ``micro_batch`` sequences that flow through ``slots`` device buffers:
-    the host->device copy of one group, the fused prefill of the previous one
+    the host->device copy of one group, the prefill of the previous one
     and the device->host copy of the one before run on three streams at once
     (the two copy directions use separate copy engines). By default a group
     holds enough sequences for its q copy to reach 64 MiB, and at most half
@@ -438,7 +438,7 @@ def fa_kla_prefill_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weigh
                     pipe.bt[sl][:n].copy_(temp[b0:b1], non_blocking=True)
             in_done = torch.cuda.Event()
             in_done.record(s_in)
-            # fused prefill on the caller's stream (slot output free once copied out)
+            # prefill on the caller's stream (slot output free once copied out)
             main.wait_event(in_done)
             if pipe.out_free[sl] is not None:
                 main.wait_event(pipe.out_free[sl])

@@ -220,7 +220,7 @@ class LearnablePositiveMap(FeatureMap):
         self.mlp = nn.Sequential(*layers)
         self.num_layers = num_layers
 
-    # -- what the fused FA-KLA kernels need
+    # -- what the one-call FA-KLA entry points need
     @property
     def fusable(self) -> bool:
         """True when phi is exactly one linear layer followed by elu+1."""
