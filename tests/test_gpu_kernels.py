@@ -68,6 +68,9 @@ def test_device_status_clean(cuda):
     (130, 4096, 512, 4, True, False),
     (4096, 2048, 2048, 16, True, True),
     (5000, 1024, 512, 4, False, True),    # ragged last row tile
+    (32, 4096, 4096, 32, True, True),     # small row sets: 64-row A stages, 8 stages
+    (64, 2048, 2048, 16, True, False),    # ... at their largest
+    (65, 2048, 2048, 16, True, True),     # one row past them: the plain 128-row tile
 ])
 def test_phi_bf16_tensor_core(cuda, rows, K, N, heads, use_bias, use_temp):
     from pulsartecture_b200.backend.interface import phi_map
@@ -273,10 +276,11 @@ def test_decode_general_head_dims(cuda):
     assert rel_l2(to_np(out), eo) < F32_REL_L2 and rel_l2(to_np(S), eS) < 1e-6
 
 
-def test_decode_fused_phi_bf16(cuda):
+@pytest.mark.parametrize("N,H", [(256, 4), (32, 32)])  # (32, 32): one GPU's share of an 8-way decode split
+def test_decode_fused_phi_bf16(cuda, N, H):
     from pulsartecture_b200.backend.interface import fa_kla_decode_step
 
-    N, H, Dk, M = 256, 4, 128, 128
+    Dk, M = 128, 128
     in_dim = H * Dk
     q = _normal((N, in_dim), 60, cuda, torch.bfloat16, 1 / np.sqrt(Dk))
     k = _normal((N, in_dim), 61, cuda, torch.bfloat16, 1 / np.sqrt(Dk))
