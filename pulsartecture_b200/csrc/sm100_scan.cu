@@ -4,13 +4,14 @@
 // Q = phi(q), K = phi(k)*temp, V:
 //
 //   P   = Q K^T                      (128x128 fp32, TMEM)            [MMA1]
-//   Pm  = causal_mask_inclusive(P)   split into bf16 hi + lo, in place in TMEM
+//   Pm  = causal_mask_inclusive(P)   as bf16 in place in TMEM (the backward
+//                                    modes: bf16 hi + lo residual)
 //   O   = Q S_{<c}                   (S_{<c} as bf16 in smem)        [MMA2]
 //   Dz  = Q [z_hi z_lo]              (z_{<c} split hi/lo, N = 16)    [MMA2b]
 //   S  += K^T V                      (fp32, lives in TMEM)           [MMA4]
 //   z  += K^T 1                      (fp32, N = 16, column 0)        [MMA4b]
-//   O  += Pm_hi V + Pm_lo V          (A operand straight from TMEM)  [MMA3]
-//   out = O / (rowsum(Pm) + Dz[0] + Dz[1] + 1e-12)
+//   O  += Pm V  (backward: Pm_hi V + Pm_lo V; A straight from TMEM) [MMA3]
+//   out = O / (rowsum(Pm) + Dz[0] + Dz[1] + 1e-12), the row sum in fp32
 //
 // This is the chunk-parallel form of the reference recurrence
 // (ultra_rwka/backend/cpp/cpu/cpu_kernels.cpp:107-164): out_t sums k~_s v_s
@@ -20,7 +21,7 @@
 // Warp roles (448 threads): warp 0 TMA producer (Q, K, V tiles, 2 stages);
 // warp 1 TMEM allocator + single-thread MMA issuer; three warpgroups, each
 // thread owning one TMEM lane (token r for P/O, feature r for S/z):
-//   warps 2-5   (P)  inclusive mask + hi/lo split of P, row sums; k*temp
+//   warps 2-5   (P)  inclusive mask, bf16 P (and its residual), row sums
 //   warps 6-9   (S)  state refresh: S (TMEM fp32) -> bf16 smem operand,
 //                    z -> hi/lo operand; initial state in, final state out
 //   warps 10-13 (O)  normalise O into a dead tile of the chunk and TMA-store
@@ -237,7 +238,7 @@ __device__ __forceinline__ void put_zk(uint8_t* m0, int f, float zf) {
 // The kept values first get `arow` (a per-row term) and bcol[s - sbase] (a
 // per-column term: 32 floats in shared memory, the same for every row).
 // Returns the sum of the kept values.
-template <int kMask, bool kCol, bool kRow>
+template <int kMask, bool kCol, bool kRow, bool kLo = true>
 __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase, int r,
                                              uint32_t p_addr, float arow, const float* bcol) {
   uint32_t hi[16], lo[16];
@@ -263,21 +264,21 @@ __device__ __forceinline__ float split_group(const uint32_t (&v)[32], int sbase,
     const float2 xf = f2_split(x);
     rs += xf.x + xf.y;
     hi[e] = pack_bf16x2(xf.x, xf.y);
-    lo[e] = pack_bf16x2(f2_sub(x, f2_from_bf16x2(hi[e])));
+    if (kLo) lo[e] = pack_bf16x2(f2_sub(x, f2_from_bf16x2(hi[e])));
   }
   tmem_st16(p_addr + (uint32_t)sbase, hi);
-  tmem_st16(p_addr + (uint32_t)(sbase + 16), lo);
+  if (kLo) tmem_st16(p_addr + (uint32_t)(sbase + 16), lo);
   return rs;
 }
 
 // Row r of P, token group g (32 tokens) of a warp whose rows are the group
 // q4. Causal: groups below the diagonal are kept whole, the diagonal one is
 // masked. Reversed: groups above the diagonal are kept whole.
-template <bool kRev, bool kCol, bool kRow>
+template <bool kRev, bool kCol, bool kRow, bool kLo = true>
 __device__ __forceinline__ float split_group_at(const uint32_t (&v)[32], int g, int q4, int r,
                                                 uint32_t p_addr, float arow, const float* bcol) {
-  return g == q4 ? split_group<kRev ? 2 : 1, kCol, kRow>(v, 32 * g, r, p_addr, arow, bcol)
-                 : split_group<0, kCol, kRow>(v, 32 * g, r, p_addr, arow, bcol);
+  return g == q4 ? split_group<kRev ? 2 : 1, kCol, kRow, kLo>(v, 32 * g, r, p_addr, arow, bcol)
+                 : split_group<0, kCol, kRow, kLo>(v, 32 * g, r, p_addr, arow, bcol);
 }
 
 // Outside the kept triangle the whole group is masked: hi = lo = 0.
@@ -484,6 +485,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
   // waits for the output stores of the chunk two back, so those stores stay
   // off the path to the next MMA1.
   constexpr bool kSplitV = MODE == kScanNormal;
+  // P enters MMA3 as bf16 hi + lo (the residual) in the backward modes, whose
+  // products cancel to small results, and as bf16 alone in the forward: one
+  // MMA3 per K step and no residual in the split (the split's instructions sit
+  // on the chunk's critical chain). The forward's error against the oracle
+  // stays within the bf16 bar: 2.4e-3 rel-L2 at config 2 against 1.6e-3 with
+  // the residual (bar 5e-3), max-abs 1e-3 (bar 2e-2).
+  constexpr bool kPLo = MODE != kScanNormal;
   // Vectors shared by every row of a chunk, broadcast from shared memory in
   // the unused rows of the two 1 KB N=16 operand atoms (with kZ, rows 0-1 of
   // both hold ZK and rows 4-5 of M0 ONES; the other rows only feed result
@@ -714,13 +722,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         ok = bar_wait(&bars[kE1Done], par, kWaitNs);
         if (!ok) break;
         tc_fence_after();
-        // MMA3: O += Pm_hi V + Pm_lo V. Hi/lo of tokens [32g, 32g+32) sit in
-        // columns 32g + [0,16) and 32g + [16,32); K step j = 16 tokens.
+        // MMA3: O += Pm_hi V (+ Pm_lo V in the backward modes). Hi/lo of
+        // tokens [32g, 32g+32) sit in columns 32g + [0,16) and 32g + [16,32);
+        // K step j = 16 tokens.
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t col = kColP + (uint32_t)(32 * (j >> 1) + 8 * (j & 1));
           mma_ts(tmem + kColO, tmem + col, mndesc(aV, j), idPV, 1u);
-          mma_ts(tmem + kColO, tmem + col + 16u, mndesc(aV, j), idPV, 1u);
+          if constexpr (kPLo) mma_ts(tmem + kColO, tmem + col + 16u, mndesc(aV, j), idPV, 1u);
         }
         if constexpr (MODE == kScanRevCol) {
           if (args.vec_mma) {
@@ -803,11 +812,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_sm100_kernel(
         if (k1) tmem_ld32(p_addr + (uint32_t)(32 * g0 + 32), vb);
         tmem_ld_wait();
         if (k0)
-          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd>(va, g0, q4, r, p_addr, arow, bcol_sm + 32 * g0);
+          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd, kPLo>(va, g0, q4, r, p_addr, arow, bcol_sm + 32 * g0);
         else
           zero_group(g0, p_addr);
         if (k1)
-          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd>(vb, g0 + 1, q4, r, p_addr, arow, bcol_sm + 32 * g0 + 32);
+          rs += split_group_at<kRev, kCol, MODE == kScanRowAdd, kPLo>(vb, g0 + 1, q4, r, p_addr, arow, bcol_sm + 32 * g0 + 32);
         else
           zero_group(g0 + 1, p_addr);
       }
