@@ -298,6 +298,48 @@ def test_decode_fused_phi_bf16(cuda, N, H):
     assert rel_l2(to_np(S), eS) < BF16_REL_L2 and rel_l2(to_np(z), ez) < BF16_REL_L2
 
 
+@pytest.mark.parametrize("N,H", [(32, 32), (64, 32), (128, 32), (129, 32), (20, 16)])
+def test_decode_map_rows_against_oracle(cuda, N, H):
+    """The decode step's feature map, read back from the caller's workspace,
+    against the oracle at the half-ulp bar, with the k-side temperature, for
+    the few-sequence row sets of a split decode batch (fewer than 128 rows per
+    A box, one row tile, and one row past it). The step's outputs are checked
+    too."""
+    from pulsartecture_b200 import _lib
+
+    L = _lib.lib()
+    Dk = M = 128
+    in_dim = H * Dk
+    q = _normal((N, in_dim), 70, cuda, torch.bfloat16, 1 / np.sqrt(Dk))
+    k = _normal((N, in_dim), 71, cuda, torch.bfloat16, 1 / np.sqrt(Dk))
+    v = _normal((N, H, M), 72, cuda, torch.bfloat16, 1 / np.sqrt(Dk))
+    temp = _phi_like((N, H), 73, cuda, torch.bfloat16)
+    W, b = lpm_params(in_dim, H * M, seed=74, dtype=torch.bfloat16)
+    W, b = W.to(cuda), b.to(cuda)
+    S = _normal((N, H, M, M), 75, cuda, torch.float32, 0.02)
+    z = _phi_like((N, H, M), 76, cuda, torch.float32)
+    S0, z0 = to_np(S), to_np(z)
+    out = torch.empty(N, H, M, device=cuda, dtype=torch.bfloat16)
+    wsb = L.fakla_decode_workspace_bytes(N, in_dim, H, M, M, _lib.FAKLA_BF16)
+    ws = torch.zeros(wsb, device=cuda, dtype=torch.uint8)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.fakla_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), temp.data_ptr(), W.data_ptr(), b.data_ptr(),
+                              out.data_ptr(), S.data_ptr(), z.data_ptr(), N, in_dim, H, M, M, _lib.FAKLA_BF16,
+                              ws.data_ptr(), wsb, stream))
+    _lib.check(L.fakla_device_status(stream))
+    one = N * H * M * 2
+    phq = ws[:one].view(torch.bfloat16).view(N, H * M)
+    phk = ws[wsb // 2:wsb // 2 + one].view(torch.bfloat16).view(N, H * M)
+    eq = O.phi(to_np(q), to_np(W), to_np(b), None, H)
+    ek = O.phi(to_np(k), to_np(W), to_np(b), to_np(temp), H)
+    for got, exp in ((phq, eq), (phk, ek)):
+        g = to_np(got)
+        assert np.all(np.abs(g - exp) <= 2.0 ** -8 * np.abs(exp) + 1e-4)
+    eo, eS, ez = O.decode_step(eq.reshape(N, H, M), ek.reshape(N, H, M), to_np(v), S0, z0)
+    assert rel_l2(to_np(out), eo) < BF16_REL_L2 and np.abs(to_np(out) - eo).max() < BF16_MAX_ABS
+    assert rel_l2(to_np(S), eS) < BF16_REL_L2 and rel_l2(to_np(z), ez) < BF16_REL_L2
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_zero_tokens(cuda, dtype):
     """T = 0 (and B = 0): an empty output, and the state of zero tokens — the
