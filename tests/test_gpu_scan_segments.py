@@ -119,3 +119,42 @@ def test_long_context_b1h32t65536_full_size(cuda):
         assert rel_l2(got, eo) < BF16_REL_L2
         assert np.abs(got - eo).max() < BF16_MAX_ABS
         assert rel_l2(to_np(S[:, hh:hh + 1]), eS) < BF16_REL_L2
+
+
+@pytest.mark.parametrize("B,h0,h1", [
+    (1, 0, 16),   # one GPU's part of an 8-way batch split of B=8, H=16: 16 sequences, 8 segments of 4 chunks
+    (2, 0, 16),   # ... of a 4-way batch split: 32 sequences, 4 segments of 8 chunks
+    (8, 6, 8),    # ... of an 8-way head split (heads 6-7, the map's rows of those heads, q and k rows whole)
+])
+def test_prefill_shard_shapes_against_oracle(cuda, B, h0, h1):
+    """fa_kla at the per-GPU shapes of the multi-GPU prefill bench (T=4096,
+    D=M=128, bf16, LearnablePositiveMap(2048 -> 2048) rows of the shard's
+    heads, with temperature): the scan runs segmented, and two sequences are
+    checked against the oracle fed the oracle's own phi."""
+    from pulsartecture_b200.attention import fa_kla
+
+    T, H, D = 4096, 16, 128
+    Hs = h1 - h0
+    g = torch.Generator(device=cuda).manual_seed(140 + B + h0)
+    q = (torch.randn(B, T, H * D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    k = (torch.randn(B, T, H * D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    v = (torch.randn(B, T, Hs, D, generator=g, device=cuda) / np.sqrt(D)).bfloat16()
+    tp = (torch.rand(B, T, Hs, generator=g, device=cuda) + 0.5).bfloat16()
+    W, b = lpm_params(H * D, H * D, seed=0, dtype=torch.bfloat16)
+    Ws, bs = W[h0 * D:h1 * D].contiguous().to(cuda), b[h0 * D:h1 * D].contiguous().to(cuda)
+    from pulsartecture_b200 import _lib
+
+    assert _lib.lib().fakla_attention_workspace_bytes(B, T, Hs, D, D, _lib.FAKLA_BF16) > 0, "segmented"
+    out, (S, z) = fa_kla(q, k, v, phi_weight=Ws, phi_bias=bs, temp=tp)
+    assert torch.isfinite(out).all() and torch.isfinite(S).all()
+    for bb, hh in [(0, 0), (B - 1, Hs - 1)]:
+        Wh, bh = to_np(Ws)[hh * D:(hh + 1) * D], to_np(bs)[hh * D:(hh + 1) * D]
+        pq = O.phi(to_np(q[bb]), Wh, bh)
+        pk = O.phi(to_np(k[bb]), Wh, bh)
+        eo, eS, ez = O.attention(pq[None, :, None], pk[None, :, None], to_np(v[bb, :, hh])[None, :, None],
+                                 to_np(tp[bb, :, hh])[None, :, None])
+        got = to_np(out[bb, :, hh])
+        assert rel_l2(got, eo[0, :, 0]) < BF16_REL_L2
+        assert np.abs(got - eo[0, :, 0]).max() < BF16_MAX_ABS
+        assert rel_l2(to_np(S[bb, hh]), eS[0, 0]) < BF16_REL_L2
+        assert rel_l2(to_np(z[bb, hh]), ez[0, 0]) < BF16_REL_L2
