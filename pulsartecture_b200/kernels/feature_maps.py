@@ -17,7 +17,6 @@ from __future__ import annotations
 import math
 import warnings
 from abc import ABC, abstractmethod
-from typing import Optional
 
 import torch
 import torch.nn as nn

@@ -1,7 +1,6 @@
 """The gradient oracle (float64 torch restatement, CPU): its forward equals
 the C oracle (itself pinned to the reference), and its autograd gradients
 equal finite differences (torch.autograd.gradcheck)."""
-import numpy as np
 import torch
 
 from oracle import fakla_grad_oracle as G
