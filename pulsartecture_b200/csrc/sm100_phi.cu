@@ -26,9 +26,9 @@
 //
 // Large GEMMs run the same kernel as CTA pairs (clusters of two): a pair
 // computes a 256x256 tile with cta_group::2 MMAs (256x256x16) issued by rank
-// 0; each CTA loads its 128 x rows and 128 of the tile's 256 W rows per stage
-// (6 stages of 32 KB), so each SM moves a third fewer operand bytes per FLOP
-// through L2 and shared memory. Rank 0's commits arrive on both CTAs'
+// 0; each CTA loads its 128 x rows and 128 of the tile's 256 W rows for two
+// 64-wide K slabs per stage (3 stages of 64 KB), so each SM moves a third
+// fewer operand bytes per FLOP through L2 and shared memory. Rank 0's commits arrive on both CTAs'
 // barriers; each CTA runs the epilogue of its own 128 rows from its own TMEM.
 //
 // A persistent grid gives every pair the tiles tile0, tile0 + pairs, ...; when
@@ -59,9 +59,18 @@ constexpr int kABytes = BM * BK * 2;                 // 16 KB
 // Per CTA: a single CTA holds all BNT rows of the W tile; a CTA pair splits them.
 template <int BNT, bool PAIR> constexpr int kBRowsT = PAIR ? BNT / 2 : BNT;
 template <int BNT, bool PAIR> constexpr int kBBytesT = kBRowsT<BNT, PAIR> * BK * 2;
-template <int BNT, bool PAIR> constexpr int kStageBytesT = kABytes + kBBytesT<BNT, PAIR>;
-// 4 stages of 48 KB (single CTA, BNT 256) or 6 of 32 KB (pair, BNT 256)
-template <int BNT, bool PAIR> constexpr int kStagesT = PAIR ? 6 : 4;
+// K slabs of BK per pipeline stage. One thread issues every MMA, and each
+// MMA instruction takes it about 70 cycles to issue while each stage adds a
+// barrier wait and a commit (about 300 cycles): with one slab a CTA pair's
+// four 256x256x16 MMAs (128 cycles of tensor pipe each) could not be issued
+// as fast as the pipe ran them. Two slabs put eight MMAs behind each round
+// trip. Single CTAs and the MN-major forms keep one slab.
+template <int BNT, bool PAIR, bool AMN, bool BMN>
+constexpr int kSlabsT = (PAIR && !AMN && !BMN) ? 2 : 1;
+template <int BNT, bool PAIR, int SL> constexpr int kStageBytesT = SL * (kABytes + kBBytesT<BNT, PAIR>);
+// 4 stages of 48 KB (single CTA, BNT 256), 6 of 32 KB (pair, one slab) or
+// 3 of 64 KB (pair, two slabs)
+template <int BNT, bool PAIR, int SL> constexpr int kStagesT = PAIR ? (SL == 2 ? 3 : 6) : 4;
 constexpr int kEpiWarps = 8;
 constexpr int kOutWarpBytes = 32 * 128;              // 32 rows x 64 bf16
 constexpr int kOutBytes = kEpiWarps * kOutWarpBytes;  // 32 KB (one buffer per warp)
@@ -74,9 +83,9 @@ constexpr uint64_t kWaitNs = 2000000000ull;          // 2 s per wait
 // producer, the MMA issuer and the epilogue's poller spend few issue slots.
 constexpr uint32_t kSleepNs = 50000;
 
-template <int BNT, bool PAIR>
+template <int BNT, bool PAIR, int SL = 1>
 constexpr size_t kSmemBytesT = 1024 /*align slack*/ +
-                               (size_t)kStagesT<BNT, PAIR> * kStageBytesT<BNT, PAIR> + kOutBytes + 256;
+                               (size_t)kStagesT<BNT, PAIR, SL> * kStageBytesT<BNT, PAIR, SL> + kOutBytes + 256;
 
 // x - 2 pi k with k = round(x / (2 pi)): the cos/sin argument brought into
 // [-pi, pi] (Cody-Waite reduction with 2 pi split into a float head and the
@@ -132,13 +141,16 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  constexpr int kStages = kStagesT<BNT, PAIR>;
+  constexpr int SL = kSlabsT<BNT, PAIR, AMN, BMN>;
+  constexpr int kStages = kStagesT<BNT, PAIR, SL>;
   constexpr int kBBytes = kBBytesT<BNT, PAIR>;
+  constexpr int kAStage = SL * kABytes;  // A bytes per stage (SL slabs of kABytes)
+  constexpr int kBStage = SL * kBBytes;
   constexpr uint32_t kTmemCols = kTmemColsT<BNT>;
   constexpr int kTileRows = PAIR ? 2 * BM : BM;
-  uint8_t* sA = smem;                                  // kStages x 16 KB
-  uint8_t* sB = smem + kStages * kABytes;              // kStages x kBBytes
-  uint8_t* sOut = sB + kStages * kBBytes;              // 32 KB (1024-aligned)
+  uint8_t* sA = smem;                                  // kStages x kAStage
+  uint8_t* sB = smem + kStages * kAStage;              // kStages x kBStage
+  uint8_t* sOut = sB + kStages * kBStage;              // 32 KB (1024-aligned)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
   uint64_t* full = bars;                  // [kStages]
   uint64_t* empty = bars + kStages;       // [kStages]
@@ -158,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
   const int col_tiles = args.N / BNT;
   const int tiles_per_set = row_tiles * col_tiles;
   const int total_tiles = tiles_per_set * args.nsets;
-  const int kblocks = (args.K + BK - 1) / BK;  // a ragged last block reads zeros past K
+  // stages of SL * BK along K; a ragged last one reads zeros past K
+  const int kblocks = (args.K + SL * BK - 1) / (SL * BK);
   // work units: whole tiles [0, n_full), then each remaining tile as two
   // halves of BNT / 2 columns (CTA pairs only; the host passes n_full =
   // total_tiles otherwise)
@@ -216,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
     if (args.a_rows < BM) {
       const int from = args.a_rows * 128 / 16, to = BM * 128 / 16;  // uint4 offsets within a stage
       for (int s = 0; s < kStages; ++s) {
-        uint4* dst = reinterpret_cast<uint4*>(sA + s * kABytes);
+        uint4* dst = reinterpret_cast<uint4*>(sA + s * kAStage);  // one slab (single CTAs)
         for (int o = from + (int)threadIdx.x; o < to; o += kThreads) dst[o] = make_uint4(0u, 0u, 0u, 0u);
       }
       fence_proxy_async_smem();
@@ -259,20 +272,24 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             *abort_flag = 1;
             break;
           }
-          uint8_t* dA = sA + stage * kABytes;
-          uint8_t* dB = sB + stage * kBBytes;
+          uint8_t* dA = sA + stage * kAStage;
+          uint8_t* dB = sB + stage * kBStage;
           if constexpr (PAIR) {
             const uint32_t fb = mapa_shared(&full[stage], 0);
-            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * stage_tx);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * SL * stage_tx);
             if constexpr (AMN) {
               for (int a = 0; a < BM / 64; ++a) tma_load_2d_pair(dA + a * kMnAtom, mapA, fb, row0 + 64 * a, kb * BK);
             } else {
-              tma_load_2d_pair(dA, mapA, fb, kb * BK, row0);
+#pragma unroll
+              for (int sl = 0; sl < SL; ++sl)
+                tma_load_2d_pair(dA + sl * kABytes, mapA, fb, (kb * SL + sl) * BK, row0);
             }
             if constexpr (BMN) {
               for (int a = 0; a < brows / 64; ++a) tma_load_2d_pair(dB + a * kMnAtom, mapB, fb, col0 + 64 * a, kb * BK);
             } else {
-              tma_load_2d_pair(dB, mapB, fb, kb * BK, col0);
+#pragma unroll
+              for (int sl = 0; sl < SL; ++sl)
+                tma_load_2d_pair(dB + sl * kBBytes, mapB, fb, (kb * SL + sl) * BK, col0);
             }
           } else {
             mbar_arrive_expect_tx(&full[stage], stage_tx);
@@ -333,14 +350,20 @@ __global__ void __launch_bounds__(kThreads, 1) phi_gemm_sm100_kernel(
             break;
           }
           tc_fence_after();
-          const uint64_t da = smem_desc_sw128(smem_u32(sA + stage * kABytes), AMN ? kMnAtom : 16, 1024);
-          const uint64_t db = smem_desc_sw128(smem_u32(sB + stage * kBBytes), BMN ? kMnAtom : 16, 1024);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            if constexpr (PAIR)
-              mma_ss_pair(d_tmem, da + kStepA * k, db + kStepB * k, idesc, (kb | k) != 0 ? 1u : 0u);
-            else
-              mma_ss(d_tmem, da + kStepA * k, db + kStepB * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int sl = 0; sl < SL; ++sl) {
+            const uint64_t da =
+                smem_desc_sw128(smem_u32(sA + stage * kAStage + sl * kABytes), AMN ? kMnAtom : 16, 1024);
+            const uint64_t db =
+                smem_desc_sw128(smem_u32(sB + stage * kBStage + sl * kBBytes), BMN ? kMnAtom : 16, 1024);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint32_t accum = (kb | sl | k) != 0 ? 1u : 0u;
+              if constexpr (PAIR)
+                mma_ss_pair(d_tmem, da + kStepA * k, db + kStepB * k, idesc, accum);
+              else
+                mma_ss(d_tmem, da + kStepA * k, db + kStepB * k, idesc, accum);
+            }
           }
           if constexpr (PAIR)
             mma_commit_pair(&empty[stage]);
@@ -578,7 +601,7 @@ static int pair_slots() {
     int n = 0;
     const auto kern = phi_gemm_sm100_kernel<FAKLA_ACT_ELU1, BN, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBytesT<BN, true>) == cudaSuccess) {
+                             (int)kSmemBytesT<BN, true, kSlabsT<BN, true, false, false>>) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -587,7 +610,7 @@ static int pair_slots() {
       attr[0].val.clusterDim.z = 1;
       cfg.gridDim = dim3(2 * fakla_sm_count());
       cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = kSmemBytesT<BN, true>;
+      cfg.dynamicSmemBytes = kSmemBytesT<BN, true, kSlabsT<BN, true, false, false>>;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
@@ -642,17 +665,17 @@ static int64_t whole_tiles(int64_t tiles, int tiling) {
 template <int ACT, int BNT, bool PAIR, bool AMN = false, bool BMN = false>
 static cudaError_t launch_act_t(const PhiMaps& m, const PhiArgs& a, int64_t units, cudaStream_t stream) {
   const auto kern = phi_gemm_sm100_kernel<ACT, BNT, PAIR, AMN, BMN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytesT<BNT, PAIR>);
+  constexpr size_t smem = kSmemBytesT<BNT, PAIR, kSlabsT<BNT, PAIR, AMN, BMN>>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if constexpr (PAIR) {
     const int64_t pairs = units < pair_slots() ? units : pair_slots();
-    return launch_chained(kern, dim3((unsigned)(2 * pairs)), dim3(kThreads), kSmemBytesT<BNT, PAIR>, stream,
+    return launch_chained(kern, dim3((unsigned)(2 * pairs)), dim3(kThreads), smem, stream,
                           2u, m.A0, m.A1, m.B, m.Bh, m.C0, m.C1, a);
   } else {
     const int sms = fakla_sm_count();
     const int grid = units < sms ? (int)units : sms;
-    return launch_chained(kern, dim3((unsigned)grid), dim3(kThreads), kSmemBytesT<BNT, PAIR>, stream, 1u,
+    return launch_chained(kern, dim3((unsigned)grid), dim3(kThreads), smem, stream, 1u,
                           m.A0, m.A1, m.B, m.Bh, m.C0, m.C1, a);
   }
 }
